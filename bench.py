@@ -1,0 +1,392 @@
+#!/usr/bin/env python3
+"""Benchmark of the variable-K grouped FP8 wgrad on 1..8 B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config gate_up] [--impl ours|reference]
+
+One step = one call of the hot path over one synthetic batch: every expert's weight gradient
+C[g] = sL*sR * LHS_g^T RHS_g for the configured problem (default: BASELINE config 1,
+GPT-OSS-20B gate_up_wgrad: G=32, M_total=131072, 2880 x 5760, e4m3 x e5m2 -> bf16).
+Metric: TFLOPS = 2*M_total*OUT_M*OUT_N / time (launcher.cpp:76), whole job over all GPUs.
+
+N > 1 (launched by torchrun): expert-sharded weak scaling. Every rank owns its own
+gate_up-shaped shard (32 experts, 131072 tokens, 2880 x 5760) of a 32N-expert problem and runs
+the kernel on it; there is no collective on the timed path (the barrier and the max-over-ranks
+reduction sit outside the timed region). ``--config shard120b`` instead partitions the
+GPT-OSS-120B-shaped problem (G=128, M_total=1048576) contiguously across the N ranks.
+
+Timing: W untimed warm-up steps, then K steps between CUDA events on the launching stream,
+bracketed by a barrier and torch.cuda.synchronize(); the time is the max over ranks. The
+operands (1.13 GB for gate_up) are far larger than the 126 MB L2, so no L2 flush is needed.
+
+--impl reference: the reference's own implementation of the path cannot run here (AMD gfx950
+code object + a Triton kernel from the absent primus_turbo package), so the reference arm
+times the CPU restatement of its algorithm (oracle/, torch fp32 dequantise + matmul per expert)
+on all host threads, one expert per step, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+REF_PUBLISHED_TFLOPS = 1237.0  # MI355X, hand-optimised ASM, gate_up_wgrad (README.md:60)
+FP8_NOMINAL_TFLOPS = 4500.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="gate_up",
+                    choices=["gate_up", "down", "skew", "shard120b", "ref_exp"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="approximate CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    """(fp8 dense peak TFLOP/s, hbm GB/s, description). FP8 = 2x the measured bf16 cuBLAS burst
+    figure (the B200 tensor core runs fp8 at twice the bf16 rate)."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return (2.0 * float(d["bf16_tflops"]), float(d["hbm_gbs"]),
+                "of measured: 2 x MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst)")
+    return 2.0 * 1590.0, 6650.0, "of fallback: 2 x 1.59 PFLOP/s bf16"
+
+
+def profile_traffic(workload: str):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary, or None."""
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    d = json.loads(f.read_text())
+    ent = d.get(workload)
+    return None if ent is None else float(ent["dram_bytes_per_launch"])
+
+
+class ClockSampler:
+    """nvidia-smi sampler for the timed region (clocks and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        busy = [x for x in sm if smax and x > 0.3 * smax] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def build_problem(args, rank, world, device):
+    from ggemm_asm_b200 import inputs, sharding
+
+    if args.config == "shard120b":
+        lens = inputs.config_lens("shard120b", args.seed)
+        shards = sharding.partition(lens, world)
+        sh = shards[rank]
+        full = inputs.offsets_from_lens(lens)
+        p = inputs.make_problem("shard120b", seed=args.seed, device=device, lens=lens,
+                                rows=(sh.t_begin, sh.t_end))
+        loc = sharding.local_offsets(full, sh)
+        return inputs.Problem(
+            name=f"shard120b[{sh.g_begin}:{sh.g_end}]", G=sh.groups, M_total=sh.tokens,
+            OUT_M=p.OUT_M, OUT_N=p.OUT_N, lens=lens[sh.g_begin:sh.g_end], offs=loc,
+            lhs=p.lhs, rhs=p.rhs, lhs_scale=p.lhs_scale, rhs_scale=p.rhs_scale,
+            group_offs=torch.from_numpy(loc.copy()).to(device)), "strong"
+    name = {"ref_exp": "gate_up"}.get(args.config, args.config)
+    seed = args.seed + 1000 * rank  # each rank owns a distinct shard of the 32N-expert job
+    if args.config == "ref_exp":
+        lens = inputs.reference_exponential_lens(32, 131072, 42)
+        p = inputs.make_problem("gate_up", seed=seed, device=device, lens=lens)
+    else:
+        p = inputs.make_problem(name, seed=seed, device=device)
+    return p, "weak"
+
+
+def cpu_oracle_rate(p_cpu, budget_s: float, steps: int | None = None):
+    """Time the oracle (torch CPU fp32, all threads) on whole experts; returns (TFLOPS, sample)."""
+    from oracle import vark_oracle as vo
+
+    order = np.argsort(-p_cpu.lens)  # big experts first: fewer, longer matmuls
+    done_flops, t_total, groups = 0.0, 0.0, []
+    for i, g in enumerate([int(x) for x in order if p_cpu.lens[x] > 0]):
+        t0 = time.perf_counter()
+        vo.wgrad_torch(p_cpu.lhs, p_cpu.rhs, p_cpu.lhs_scale, p_cpu.rhs_scale, p_cpu.group_offs,
+                       groups=[g])
+        t_total += time.perf_counter() - t0
+        done_flops += 2.0 * float(p_cpu.lens[g]) * p_cpu.OUT_M * p_cpu.OUT_N
+        groups.append(g)
+        if (steps is not None and i + 1 >= steps) or (steps is None and t_total >= budget_s):
+            break
+    sample = (f"{len(groups)} of {p_cpu.G} experts ({int(sum(p_cpu.lens[groups]))} tokens) of "
+              f"the same problem, torch CPU fp32 dequantise+matmul per expert")
+    return done_flops / t_total / 1e12, sample, t_total
+
+
+def run_reference(args):
+    """Reference arm: the CPU restatement of the reference algorithm, rank 0 only."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from ggemm_asm_b200 import inputs
+    from oracle import vark_oracle as vo
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    name = "gate_up" if args.config in ("ref_exp", "shard120b") else args.config
+    p = inputs.make_problem(name, seed=args.seed, device="cpu")
+    live = [int(g) for g in np.argsort(-p.lens) if p.lens[g] > 0]
+    for i in range(args.warmup):
+        vo.wgrad_torch(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, groups=[live[i % len(live)]])
+    flops, t = 0.0, 0.0
+    for i in range(args.steps):
+        g = live[i % len(live)]
+        t0 = time.perf_counter()
+        vo.wgrad_torch(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, groups=[g])
+        t += time.perf_counter() - t0
+        flops += 2.0 * float(p.lens[g]) * p.OUT_M * p.OUT_N
+    v = flops / t / 1e12
+    cores = torch.get_num_threads()
+    sample = f"one expert per step (experts in size order) of config {name}"
+    line = {"impl": "reference", "metric": f"{name}_wgrad FP8 TFLOPS (CPU restatement)",
+            "value": v, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{name}_wgrad", "G": p.G, "M_total": p.M_total,
+                       "OUT_M": p.OUT_M, "OUT_N": p.OUT_N},
+            "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference kernel unavailable here (AMD gfx950 code object; primus_turbo "
+                    "Triton oracle absent); timed its algorithm restated on the CPU (oracle/)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+        pg = dist
+
+    from ggemm_asm_b200 import _lib, variable_k_wgrad
+
+    p, scaling = build_problem(args, rank, world, device)
+    out = torch.empty(p.G, p.OUT_M, p.OUT_N, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        variable_k_wgrad(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during warm-up")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- kernel-only timed region -------------------------------------------------------------
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local)
+    flops_local = p.flops
+    flops_total = flops_local if pg is None else _sum_over_ranks(pg, flops_local, device)
+    value = flops_total / (ms * 1e-3) / 1e12
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during the timed region")
+
+    # ---- end-to-end: pinned host inputs -> device -> kernel -> result back to the host ------
+    e2e = None
+    if not args.no_e2e:
+        h_lhs = torch.empty(p.lhs.shape, dtype=p.lhs.dtype, pin_memory=True)
+        h_rhs = torch.empty(p.rhs.shape, dtype=p.rhs.dtype, pin_memory=True)
+        h_ls = torch.empty(p.lhs_scale.shape, dtype=torch.float32, pin_memory=True)
+        h_rs = torch.empty(p.rhs_scale.shape, dtype=torch.float32, pin_memory=True)
+        h_offs = torch.empty(p.group_offs.shape, dtype=torch.int64, pin_memory=True)
+        for h, d in ((h_lhs, p.lhs), (h_rhs, p.rhs), (h_ls, p.lhs_scale), (h_rs, p.rhs_scale),
+                     (h_offs, p.group_offs)):
+            h.copy_(d)
+        h_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        d_lhs, d_rhs = torch.empty_like(p.lhs), torch.empty_like(p.rhs)
+        d_ls, d_rs = torch.empty_like(p.lhs_scale), torch.empty_like(p.rhs_scale)
+        d_offs = torch.empty_like(p.group_offs)
+        h2d = sum(t.numel() * t.element_size() for t in (h_lhs, h_rhs, h_ls, h_rs, h_offs))
+        d2h = h_out.numel() * h_out.element_size()
+
+        def e2e_step():
+            d_lhs.copy_(h_lhs, non_blocking=True)
+            d_rhs.copy_(h_rhs, non_blocking=True)
+            d_ls.copy_(h_ls, non_blocking=True)
+            d_rs.copy_(h_rs, non_blocking=True)
+            d_offs.copy_(h_offs, non_blocking=True)
+            variable_k_wgrad(d_lhs, d_rhs, d_ls, d_rs, d_offs, out=out)
+            h_out.copy_(out, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        e2e_steps = max(2, min(args.steps, 5))
+        barrier()
+        ev0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps)
+        e2e = {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "steps": e2e_steps}
+        if not torch.equal(h_out.to(device), out):
+            raise SystemExit("e2e output mismatch")
+
+    # ---- roofline of the dominant kernel ------------------------------------------------------
+    fp8_peak, _hbm, peak_src = measured_peaks()
+    achieved = flops_local / (ms_local * 1e-3) / 1e12
+    workload = f"{args.config}"
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+                "frac": achieved / fp8_peak, "traffic": profile_traffic(workload),
+                "peak_source": peak_src, "frac_of_nominal_4500": achieved / FP8_NOMINAL_TFLOPS,
+                "kernel": "vark_tc_kernel",
+                "algorithmic_unit": "2*tokens*OUT_M*OUT_N FLOP per launch (this rank)"}
+
+    # ---- CPU baseline (rank 0, N=1 only) --------------------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from ggemm_asm_b200 import inputs
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        pc = inputs.Problem(**{**p.__dict__}).to("cpu")
+        rate, sample, secs = cpu_oracle_rate(pc, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "TFLOPS", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": sample + f"; {secs:.1f} s", "os_cpu_count": os.cpu_count()}
+
+    if rank == 0:
+        line = {
+            "metric": "gate_up_wgrad FP8 TFLOPS (whole job) and fraction of dense FP8 peak"
+            if args.config in ("gate_up", "shard120b", "ref_exp") else f"{args.config}_wgrad FP8 TFLOPS",
+            "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": scaling,
+            "vs_baseline": (value / world) / REF_PUBLISHED_TFLOPS if args.config == "gate_up" else None,
+            "vs_baseline_note": "per-GPU value / 1237 TFLOPS (reference's best published gate_up "
+                                "number: MI355X hand-optimised ASM, README.md:60)",
+            "dtype": "fp8(e4m3 x e5m2) -> fp32 acc -> bf16",
+            "data": "synthetic (seeded N(0,1), amax-scaled fp8)",
+            "config": {"workload": f"{args.config}_wgrad", "G": p.G, "M_total": p.M_total,
+                       "OUT_M": p.OUT_M, "OUT_N": p.OUT_N, "per_rank": True,
+                       "parallelism": f"expert-shard x{world}",
+                       "l2": "inputs (1.13 GB) >> 126 MB L2; no flush"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
+            "clocks": clocks.summary(), "gpu_launches": args.steps,
+            "gpu_launches_e2e": None if e2e is None else e2e["steps"],
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def _sum_over_ranks(pg, x: float, device) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return float(t.item())
+
+
+if __name__ == "__main__":
+    main()

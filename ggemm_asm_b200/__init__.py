@@ -1,0 +1,21 @@
+"""ggemm_asm_b200 - B200 (sm_100a) variable-K grouped FP8 GEMM (MoE expert weight gradient).
+
+    C[g] = sL * sR * LHS[off_g:off_{g+1}]^T @ RHS[off_g:off_{g+1}]   (e4m3 x e5m2 -> fp32 -> bf16)
+
+Public API:
+  grouped_gemm_fp8_tensorwise_variable_k  torch entry point (mirrors the Primus-Turbo call the
+                                          ggemm-asm harness makes, bench.py:268)
+  variable_k_wgrad                        alias
+  launch_raw                              the 14-argument C-ABI drop-in with raw pointers
+  inputs / sharding                       seeded problems and expert sharding for 1..8 GPUs
+The C ABI itself is declared in include/ggemm_vark.h and lives in libggemm_vark.so.
+"""
+from .grouped_gemm import (  # noqa: F401
+    flops,
+    grouped_gemm_fp8_tensorwise_variable_k,
+    launch_raw,
+    variable_k_wgrad,
+)
+from ._lib import VarkError, read_status  # noqa: F401
+
+__version__ = "0.1.0"

@@ -1,0 +1,293 @@
+// vark_capi.cu - the C ABI (include/ggemm_vark.h): argument checks, path choice, TMA tensor
+// maps, per-device state, launch.
+//
+// Replaces the reference's launch boundary: prepare_variable_k_args / launch_variable_k_kernel
+// (ggemm-asm bench.py:364-413) and the KernelArgs packing + hipModuleLaunchKernel of
+// launcher.cpp:16-33,123-168. The reference launches a fixed grid (#CUs x 512 threads, 64 KiB
+// LDS); here the grid is one persistent CTA per SM and the geometry is internal.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/ggemm_vark.h"
+#include "vark_internal.h"
+
+namespace vark {
+cudaError_t tc_set_attributes();
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
+constexpr int64_t kTokenCoordLimit = INT32_MAX;        // TMA coordinates are int32
+
+thread_local int t_last_cuda_error = 0;
+
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t* status = nullptr;  // 256-byte block owned by the library
+};
+
+std::mutex g_mutex;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int fail_cuda(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return GGEMM_VARK_ECUDA;
+}
+
+// Resolve per-device state once (SM count, compute capability, status block, kernel
+// attributes). Returns a GGEMM_VARK_E* code.
+int get_device(DeviceState** out, int* dev_out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return GGEMM_VARK_ENO_DEVICE;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return GGEMM_VARK_ENO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& s = g_dev[dev];
+  if (!s.ready) {
+    if ((e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if (s.cc_major != 10 || s.cc_minor != 0) return GGEMM_VARK_ENO_DEVICE;  // sm_100 only
+    if ((e = vark::tc_set_attributes()) != cudaSuccess) return fail_cuda(e);
+    void* blk = nullptr;
+    if ((e = cudaMalloc(&blk, 256)) != cudaSuccess) return fail_cuda(e);
+    if ((e = cudaMemset(blk, 0, 256)) != cudaSuccess) {
+      cudaFree(blk);
+      return fail_cuda(e);
+    }
+    s.status = static_cast<uint32_t*>(blk);
+    if (g_encode == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+        return fail_cuda(e == cudaSuccess ? cudaErrorSymbolNotFound : e);
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    s.ready = true;
+  }
+  *out = &s;
+  if (dev_out) *dev_out = dev;
+  return GGEMM_VARK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool tc_layout_ok(const void* lhs, const void* rhs, void* c, int32_t OUT_M, int32_t OUT_N,
+                  int32_t slm, int32_t srm, int32_t scg, int32_t scm, int32_t scn) {
+  (void)OUT_M;
+  (void)OUT_N;
+  if (!aligned16(lhs) || !aligned16(rhs) || !aligned16(c)) return false;
+  if (slm % 16 != 0 || srm % 16 != 0) return false;              // fp8 row pitch, bytes
+  if (scn != 1) return false;                                     // C rows contiguous
+  if ((2ll * scm) % 16 != 0 || (2ll * scg) % 16 != 0) return false;  // bf16 pitches
+  return true;
+}
+
+int check_args(const void* lhs, const void* rhs, void* c, const float* ls, const float* rs,
+               const int64_t* offs, int32_t G, int32_t OUT_M, int32_t OUT_N, int32_t slm,
+               int32_t srm, int32_t scg, int32_t scm, int32_t scn) {
+  if (lhs == nullptr || rhs == nullptr || c == nullptr || ls == nullptr || rs == nullptr ||
+      offs == nullptr)
+    return GGEMM_VARK_EINVAL_PTR;
+  if (G < 0 || OUT_M <= 0 || OUT_N <= 0) return GGEMM_VARK_EINVAL_SHAPE;
+  if (slm < OUT_M || srm < OUT_N) return GGEMM_VARK_EINVAL_STRIDE;
+  if (scn <= 0 || scm <= 0 || scg <= 0) return GGEMM_VARK_EINVAL_STRIDE;
+  return GGEMM_VARK_OK;
+}
+
+CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_pitch) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_pitch};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(vark::TILE_TOKENS)};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+CUresult encode_c(CUtensorMap* map, void* c, int32_t G, int32_t OUT_M, int32_t OUT_N,
+                  int32_t scg, int32_t scm) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OUT_N), static_cast<cuuint64_t>(OUT_M),
+                              static_cast<cuuint64_t>(G)};
+  const cuuint64_t strides[2] = {2ull * static_cast<cuuint64_t>(scm),
+                                 2ull * static_cast<cuuint64_t>(scg)};
+  const cuuint32_t box[3] = {vark::EPI_BOX_COLS, vark::EPI_BOX_ROWS, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+int run(const void* lhs, const void* rhs, void* c, const float* ls, const float* rs,
+        const int64_t* offs, int32_t G, int32_t OUT_M, int32_t OUT_N, int32_t slm, int32_t srm,
+        int32_t scg, int32_t scm, int32_t scn, int64_t m_total, int32_t scale_stride,
+        int32_t path, void* status, uint64_t timeout_ns, void* stream) {
+  int rc = check_args(lhs, rhs, c, ls, rs, offs, G, OUT_M, OUT_N, slm, srm, scg, scm, scn);
+  if (rc != GGEMM_VARK_OK) return rc;
+  if (scale_stride != 0 && scale_stride != 1) return GGEMM_VARK_EINVAL_ARG;
+  if (path < GGEMM_VARK_PATH_AUTO || path > GGEMM_VARK_PATH_SIMT) return GGEMM_VARK_EINVAL_ARG;
+  if (m_total < -1) return GGEMM_VARK_EINVAL_ARG;
+  if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
+  if (G == 0) return GGEMM_VARK_OK;
+
+  DeviceState* dev = nullptr;
+  rc = get_device(&dev, nullptr);
+  if (rc != GGEMM_VARK_OK) return rc;
+
+  const int64_t token_limit =
+      m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
+  uint32_t* st = status != nullptr ? static_cast<uint32_t*>(status) : dev->status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  const bool tc_ok = tc_layout_ok(lhs, rhs, c, OUT_M, OUT_N, slm, srm, scg, scm, scn);
+  bool use_tc = tc_ok;
+  if (path == GGEMM_VARK_PATH_TCGEN05 && !tc_ok) return GGEMM_VARK_ELAYOUT;
+  if (path == GGEMM_VARK_PATH_SIMT) use_tc = false;
+
+  if (!use_tc) {
+    vark::SimtParams sp;
+    sp.lhs = static_cast<const uint8_t*>(lhs);
+    sp.rhs = static_cast<const uint8_t*>(rhs);
+    sp.c = static_cast<uint16_t*>(c);
+    sp.lhs_scale = ls;
+    sp.rhs_scale = rs;
+    sp.scale_stride = scale_stride;
+    sp.group_offs = offs;
+    sp.G = G;
+    sp.OUT_M = OUT_M;
+    sp.OUT_N = OUT_N;
+    sp.stride_lhs_m = slm;
+    sp.stride_rhs_m = srm;
+    sp.stride_cg = scg;
+    sp.stride_cm = scm;
+    sp.stride_cn = scn;
+    sp.token_limit = token_limit;
+    sp.status = st;
+    if (G > 65535) return GGEMM_VARK_ETOO_LARGE;
+    cudaError_t e = vark::simt_launch(sp, s);
+    return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
+  }
+
+  // Tensor-core path.
+  const int32_t row_tiles = (OUT_M + vark::TILE_ROWS - 1) / vark::TILE_ROWS;
+  const int32_t col_tiles = (OUT_N + vark::TILE_COLS - 1) / vark::TILE_COLS;
+  const int64_t tiles = static_cast<int64_t>(G) * row_tiles * col_tiles;
+  if (tiles > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
+
+  CUtensorMap map_rhs, map_lhs, map_c;
+  const uint64_t token_dim = static_cast<uint64_t>(token_limit);
+  if (encode_2d_u8(&map_rhs, rhs, static_cast<uint64_t>(OUT_N), token_dim,
+                   static_cast<uint64_t>(srm)) != CUDA_SUCCESS ||
+      encode_2d_u8(&map_lhs, lhs, static_cast<uint64_t>(OUT_M), token_dim,
+                   static_cast<uint64_t>(slm)) != CUDA_SUCCESS ||
+      encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm) != CUDA_SUCCESS)
+    return GGEMM_VARK_ELAYOUT;
+
+  vark::TcParams tp;
+  tp.group_offs = offs;
+  tp.lhs_scale = ls;
+  tp.rhs_scale = rs;
+  tp.scale_stride = scale_stride;
+  tp.G = G;
+  tp.OUT_M = OUT_M;
+  tp.OUT_N = OUT_N;
+  tp.row_tiles = row_tiles;
+  tp.col_tiles = col_tiles;
+  tp.token_limit = token_limit;
+  tp.status = st;
+  tp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
+  const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
+  cudaError_t e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);
+  return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* c, const float* lhs_scale,
+                         const float* rhs_scale, const int64_t* group_offs, int32_t G,
+                         int32_t OUT_M, int32_t OUT_N, int32_t stride_lhs_m,
+                         int32_t stride_rhs_m, int32_t stride_cg, int32_t stride_cm,
+                         int32_t stride_cn, void* stream) {
+  return run(lhs, rhs, c, lhs_scale, rhs_scale, group_offs, G, OUT_M, OUT_N, stride_lhs_m,
+             stride_rhs_m, stride_cg, stride_cm, stride_cn, /*m_total=*/-1, /*scale_stride=*/0,
+             GGEMM_VARK_PATH_AUTO, /*status=*/nullptr, /*timeout_ns=*/0, stream);
+}
+
+int ggemm_vark_fp8_wgrad_ex(const void* lhs, const void* rhs, void* c, const float* lhs_scale,
+                            const float* rhs_scale, const int64_t* group_offs, int32_t G,
+                            int32_t OUT_M, int32_t OUT_N, int32_t stride_lhs_m,
+                            int32_t stride_rhs_m, int32_t stride_cg, int32_t stride_cm,
+                            int32_t stride_cn, int64_t m_total, int32_t scale_stride,
+                            int32_t path, void* status, uint64_t timeout_ns, void* stream) {
+  return run(lhs, rhs, c, lhs_scale, rhs_scale, group_offs, G, OUT_M, OUT_N, stride_lhs_m,
+             stride_rhs_m, stride_cg, stride_cm, stride_cn, m_total, scale_stride, path, status,
+             timeout_ns, stream);
+}
+
+int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out) {
+  if (bits_out == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  uint32_t* blk = static_cast<uint32_t*>(status);
+  if (blk == nullptr) {
+    DeviceState* dev = nullptr;
+    const int rc = get_device(&dev, nullptr);
+    if (rc != GGEMM_VARK_OK) return rc;
+    blk = dev->status;
+  }
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail_cuda(e);
+  uint32_t words[2] = {0, 0};
+  if ((e = cudaMemcpy(words, blk, sizeof(words), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return fail_cuda(e);
+  *bits_out = words[0];
+  if (clear && (e = cudaMemset(blk, 0, 256)) != cudaSuccess) return fail_cuda(e);
+  if (clear && (e = cudaDeviceSynchronize()) != cudaSuccess) return fail_cuda(e);
+  return GGEMM_VARK_OK;
+}
+
+int ggemm_vark_tc_supported(const void* lhs, const void* rhs, void* c, int32_t OUT_M,
+                            int32_t OUT_N, int32_t stride_lhs_m, int32_t stride_rhs_m,
+                            int32_t stride_cg, int32_t stride_cm, int32_t stride_cn) {
+  return tc_layout_ok(lhs, rhs, c, OUT_M, OUT_N, stride_lhs_m, stride_rhs_m, stride_cg,
+                      stride_cm, stride_cn)
+             ? 1
+             : 0;
+}
+
+const char* ggemm_vark_strerror(int code) {
+  switch (code) {
+    case GGEMM_VARK_OK: return "success";
+    case GGEMM_VARK_EINVAL_PTR: return "a required pointer is NULL";
+    case GGEMM_VARK_EINVAL_SHAPE: return "G < 0, OUT_M <= 0 or OUT_N <= 0";
+    case GGEMM_VARK_EINVAL_STRIDE: return "a stride is not positive or is smaller than its row";
+    case GGEMM_VARK_EINVAL_ARG: return "an argument is outside its documented range";
+    case GGEMM_VARK_ENO_DEVICE: return "no CUDA device, or the current device is not sm_100";
+    case GGEMM_VARK_ECUDA: return "a CUDA runtime or driver call failed";
+    case GGEMM_VARK_ELAYOUT: return "layout cannot be expressed for the tensor-core path";
+    case GGEMM_VARK_ETOO_LARGE: return "a size exceeds the documented maximum";
+    default: return "unknown error code";
+  }
+}
+
+int ggemm_vark_last_cuda_error(void) { return t_last_cuda_error; }
+
+int ggemm_vark_version(void) { return 0x000100; }
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// vark_internal.h - host-side interface between the C ABI (vark_capi.cu) and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace vark {
+
+// Tile geometry of the tcgen05 path. One output tile is TILE_COLS columns of C (along OUT_N;
+// the MMA M dimension) by TILE_ROWS rows of C (along OUT_M; the MMA N dimension); the token
+// (reduction) dimension is consumed TILE_TOKENS rows per pipeline stage.
+constexpr int TILE_COLS = 128;
+constexpr int TILE_ROWS = 240;
+constexpr int TILE_TOKENS = 128;
+constexpr int STAGES = 4;
+constexpr int LHS_BOXES = (TILE_ROWS + 127) / 128;  // 128-wide TMA boxes per LHS stage
+
+// Per-warp C staging box of the epilogue (columns x rows), written with one TMA store.
+constexpr int EPI_BOX_COLS = 32;
+constexpr int EPI_BOX_ROWS = 16;
+
+struct TcParams {
+  const int64_t* group_offs;
+  const float* lhs_scale;
+  const float* rhs_scale;
+  int32_t scale_stride;  // 0: one scale per tensor, 1: one per group
+  int32_t G;
+  int32_t OUT_M;
+  int32_t OUT_N;
+  int32_t row_tiles;     // ceil(OUT_M / TILE_ROWS)
+  int32_t col_tiles;     // ceil(OUT_N / TILE_COLS)
+  int64_t token_limit;   // group offsets above this are invalid
+  uint32_t* status;      // device status block (bit flags in word 0)
+  uint64_t timeout_ns;   // limit on one pipeline wait
+};
+
+// Dynamic shared memory the tcgen05 kernel needs (bytes, including alignment slack).
+size_t tc_smem_bytes();
+
+// Launch the persistent tcgen05 kernel. Tensor maps are encoded by the caller.
+cudaError_t tc_launch(const CUtensorMap& map_rhs, const CUtensorMap& map_lhs,
+                      const CUtensorMap& map_c, const TcParams& p, int grid,
+                      cudaStream_t stream);
+
+struct SimtParams {
+  const uint8_t* lhs;
+  const uint8_t* rhs;
+  uint16_t* c;  // bf16 bits
+  const float* lhs_scale;
+  const float* rhs_scale;
+  int32_t scale_stride;
+  const int64_t* group_offs;
+  int32_t G, OUT_M, OUT_N;
+  int64_t stride_lhs_m, stride_rhs_m, stride_cg, stride_cm, stride_cn;
+  int64_t token_limit;
+  uint32_t* status;
+};
+
+cudaError_t simt_launch(const SimtParams& p, cudaStream_t stream);
+
+// Raise the tcgen05 kernel's dynamic shared-memory limit (once per device).
+cudaError_t tc_set_attributes();
+
+}  // namespace vark

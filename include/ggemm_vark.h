@@ -1,0 +1,134 @@
+/*
+ * ggemm_vark.h - C ABI of the B200 (sm_100a) variable-K grouped FP8 GEMM.
+ *
+ * The path computed by every entry point, for each group (expert) g in [0, G):
+ *
+ *     C[g][i][j] = bf16_rne( sL * sR * sum_{t in [off_g, off_{g+1})} LHS[t][i] * RHS[t][j] )
+ *
+ * LHS is [M_total, OUT_M] float8 e4m3fn, RHS is [M_total, OUT_N] float8 e5m2, both token-major
+ * (row t holds one token). C is [G, OUT_M, OUT_N] bf16. Products are accumulated in fp32.
+ * group_offs is a device int64 array of G+1 prefix sums (off_0 = 0, off_G = M_total); a group
+ * with off_{g+1} == off_g is empty and its C[g] is overwritten with zeros.
+ *
+ * Reference interface replaced: the 14 runtime kernel arguments of
+ * `_grouped_variable_k_gemm_kernel` (ggemm-asm README.md:88-95, launcher.cpp:16-33,
+ * bench.py:364-413): LHS, RHS, C, LHS_scale, RHS_scale, group_offs, G, OUT_M, OUT_N,
+ * stride_lhs_m, stride_rhs_m, stride_cg, stride_cm, stride_cn.  The reference's two trailing
+ * Triton scratch pointers (global_scratch, profile_scratch; always NULL there, bench.py:383-384)
+ * are dropped; the stream the reference passes as NULL (bench.py:343) is explicit here.
+ *
+ * Conventions shared by all entry points:
+ *  - every buffer is device memory owned by the caller; strides are in ELEMENTS (int32),
+ *    exactly as the reference packs them (bench.py:370-374);
+ *  - lhs_scale / rhs_scale point to device fp32 values;
+ *  - calls are asynchronous on `stream` (a cudaStream_t passed as void*, NULL = legacy default
+ *    stream); no host synchronisation and no device-to-host copy of group_offs happens;
+ *  - C is always fully overwritten (no accumulate-into-C);
+ *  - the return value is 0 on success or a GGEMM_VARK_E* code (nothing is launched on error);
+ *  - entry points are safe to call from several host threads on distinct streams.
+ */
+#ifndef GGEMM_VARK_H_
+#define GGEMM_VARK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GGEMM_VARK_API __attribute__((visibility("default")))
+#else
+#define GGEMM_VARK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------ */
+#define GGEMM_VARK_OK                 0
+#define GGEMM_VARK_EINVAL_PTR         1  /* a required pointer is NULL */
+#define GGEMM_VARK_EINVAL_SHAPE       2  /* G <= 0, OUT_M <= 0 or OUT_N <= 0 */
+#define GGEMM_VARK_EINVAL_STRIDE      3  /* a stride is not positive or makes rows overlap */
+#define GGEMM_VARK_EINVAL_ARG         4  /* another argument is out of its documented range */
+#define GGEMM_VARK_ENO_DEVICE         5  /* no CUDA device, or the current device is not sm_100 */
+#define GGEMM_VARK_ECUDA              6  /* a CUDA runtime/driver call failed */
+#define GGEMM_VARK_ELAYOUT            7  /* layout not expressible for the forced tensor-core path */
+#define GGEMM_VARK_ETOO_LARGE         8  /* a size exceeds the documented maximum */
+
+/* ---- device-side status bits (read with ggemm_vark_read_status) -------------------------- */
+#define GGEMM_VARK_DEV_BAD_OFFS   0x1u   /* group_offs not monotone, negative, or past m_total */
+#define GGEMM_VARK_DEV_TIMEOUT    0x2u   /* a pipeline wait exceeded its limit; the CTA stopped */
+
+/* ---- path selection flags for ggemm_vark_fp8_wgrad_ex ------------------------------------ */
+#define GGEMM_VARK_PATH_AUTO      0      /* tensor-core path when the layout allows, else SIMT */
+#define GGEMM_VARK_PATH_TCGEN05   1      /* force the tcgen05 path (ELAYOUT if not expressible) */
+#define GGEMM_VARK_PATH_SIMT      2      /* force the CUDA-core path (any strides) */
+
+/*
+ * ggemm_vark_fp8_wgrad - the drop-in for `_grouped_variable_k_gemm_kernel`.
+ *
+ * Replaces the launch in bench.py:364-413 (prepare_variable_k_args / launch_variable_k_kernel)
+ * and launcher.cpp:123-168 (KernelArgs + hipModuleLaunchKernel); argument order and meaning are
+ * the reference's (README.md:88-95). Per-tensor scales (one fp32 each). The token count
+ * M_total is not an argument, exactly as in the reference: group_offs is trusted to lie inside
+ * the LHS/RHS allocations. The first call on a device allocates that device's 256-byte status
+ * block (cudaMalloc); make the first call before any stream capture.
+ */
+GGEMM_VARK_API int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* c,
+                         const float* lhs_scale, const float* rhs_scale,
+                         const int64_t* group_offs,
+                         int32_t G, int32_t OUT_M, int32_t OUT_N,
+                         int32_t stride_lhs_m, int32_t stride_rhs_m,
+                         int32_t stride_cg, int32_t stride_cm, int32_t stride_cn,
+                         void* stream);
+
+/*
+ * ggemm_vark_fp8_wgrad_ex - the same computation with the extensions the reference ABI lacks.
+ *
+ *  m_total       rows allocated in LHS/RHS, or -1 if unknown. When known, group offsets past
+ *                m_total are reported (GGEMM_VARK_DEV_BAD_OFFS) and such groups are written
+ *                as zeros instead of being read.
+ *  scale_stride  0: lhs_scale/rhs_scale are single values (the reference's tensorwise scales,
+ *                bench.py:266-267); 1: they are arrays of G per-group values.
+ *  path          GGEMM_VARK_PATH_* selector.
+ *  status        device pointer to a 256-byte, 16-byte aligned status block (see
+ *                ggemm_vark_read_status), or NULL to use the library's per-device block.
+ *  timeout_ns    limit on any single pipeline wait inside the kernel (0 = default, 2 s).
+ */
+GGEMM_VARK_API int ggemm_vark_fp8_wgrad_ex(const void* lhs, const void* rhs, void* c,
+                            const float* lhs_scale, const float* rhs_scale,
+                            const int64_t* group_offs,
+                            int32_t G, int32_t OUT_M, int32_t OUT_N,
+                            int32_t stride_lhs_m, int32_t stride_rhs_m,
+                            int32_t stride_cg, int32_t stride_cm, int32_t stride_cn,
+                            int64_t m_total, int32_t scale_stride, int32_t path,
+                            void* status, uint64_t timeout_ns,
+                            void* stream);
+
+/*
+ * ggemm_vark_read_status - synchronously read (and optionally clear) the device status bits
+ * (GGEMM_VARK_DEV_*) written by earlier launches. `status` is the block given to _ex, or NULL
+ * for the current device's library block. Synchronises the device. Returns a GGEMM_VARK_E code.
+ */
+GGEMM_VARK_API int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out);
+
+/* ggemm_vark_tc_supported - 1 if `path` AUTO would take the tcgen05 path for this layout. */
+GGEMM_VARK_API int ggemm_vark_tc_supported(const void* lhs, const void* rhs, void* c,
+                            int32_t OUT_M, int32_t OUT_N,
+                            int32_t stride_lhs_m, int32_t stride_rhs_m,
+                            int32_t stride_cg, int32_t stride_cm, int32_t stride_cn);
+
+/* ggemm_vark_strerror - static description of a GGEMM_VARK_E* code. */
+GGEMM_VARK_API const char* ggemm_vark_strerror(int code);
+
+/* ggemm_vark_last_cuda_error - the CUDA error number behind the last GGEMM_VARK_ECUDA on this
+ * host thread (0 if none). */
+GGEMM_VARK_API int ggemm_vark_last_cuda_error(void);
+
+/* ggemm_vark_version - library version, e.g. 0x000100 for 0.1.0. */
+GGEMM_VARK_API int ggemm_vark_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* GGEMM_VARK_H_ */

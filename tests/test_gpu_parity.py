@@ -1,0 +1,205 @@
+"""GPU parity: the CUDA paths (through the C ABI) against the CPU oracle on identical bytes.
+
+Tolerance (stated by the north star, implemented in oracle.vark_oracle.tolerance):
+    |C - oracle| <= 1 ulp_bf16(|oracle_fp32|) + 2 * K_g * 2^-24 * sL*sR * (|LHS_g|^T |RHS_g|)
+per element, and cosine(C, oracle) >= 0.99999 over the whole output.
+"""
+import numpy as np
+import pytest
+import torch
+
+from ggemm_asm_b200 import _lib, grouped_gemm_fp8_tensorwise_variable_k as vark, inputs, launch_raw
+from oracle import vark_oracle as vo
+
+pytestmark = pytest.mark.gpu
+COS_MIN = 0.99999
+
+
+def _check(problem, out, groups=None, label=""):
+    p = problem
+    ref32 = vo.wgrad_torch_f32(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, groups)
+    tol = vo.tolerance(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, ref32, groups)
+    got = out.float().cpu()
+    if groups is not None:
+        got = got[list(groups)]
+    ref = ref32.to(torch.bfloat16).float()
+    err = (got - ref).abs()
+    bad = ~(err <= tol)
+    assert not bool(bad.any()), (
+        f"{label}: {int(bad.sum())} elements out of tolerance; max err {err.max().item():.4g}, "
+        f"first at {tuple(int(i) for i in bad.nonzero()[0])}")
+    cos = vo.cosine(got, ref32)
+    assert cos >= COS_MIN, f"{label}: cosine {cos}"
+    for i, g in enumerate(range(p.G) if groups is None else groups):
+        if p.lens[g] == 0:
+            assert bool((got[i] == 0).all()), f"{label}: empty group {g} not zero"
+    return cos, err.max().item()
+
+
+def _run(p, path="auto", out=None):
+    d = p.to("cuda")
+    o = vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, d.group_offs, out=out, path=path)
+    torch.cuda.synchronize()
+    assert _lib.read_status(clear=True) == 0
+    return o
+
+
+@pytest.mark.parametrize("path", ["tcgen05", "simt"])
+def test_tiny_config(path):
+    p = inputs.make_problem("tiny", seed=0)
+    assert p.offs.tolist() == [0, 256, 256, 768, 1024]
+    _check(p, _run(p, path), label=f"tiny/{path}")
+
+
+RAGGED = [
+    [1],
+    [31, 32, 33],
+    [127, 128, 129, 255, 256, 257],
+    [5, 0, 0, 1000, 0, 3],
+    [300, 0, 77, 160, 487],
+    [0, 0, 0],
+    [4096],
+]
+
+
+@pytest.mark.parametrize("lens", RAGGED, ids=[str(i) for i in range(len(RAGGED))])
+@pytest.mark.parametrize("path", ["tcgen05", "simt"])
+def test_ragged_groups(lens, path):
+    p = inputs.make_problem("tiny", seed=3, lens=lens, OUT_M=272, OUT_N=384)
+    _check(p, _run(p, path), label=f"ragged{lens}/{path}")
+
+
+@pytest.mark.parametrize("shape", [(240, 128), (480, 256), (16, 16), (2880, 128), (64, 5760),
+                                   (496, 400)])
+def test_tile_edges(shape):
+    OUT_M, OUT_N = shape
+    p = inputs.make_problem("tiny", seed=5, lens=[200, 57, 0, 301], OUT_M=OUT_M, OUT_N=OUT_N)
+    _check(p, _run(p, "tcgen05"), label=f"edges{shape}")
+
+
+def test_tc_equals_simt_bitwise_close():
+    p = inputs.make_problem("tiny", seed=7, lens=[700, 1, 300, 2000], OUT_M=480, OUT_N=512)
+    a = _run(p, "tcgen05").float()
+    b = _run(p, "simt").float()
+    assert vo.cosine(a, b) >= COS_MIN
+
+
+def test_per_group_scales():
+    p = inputs.make_problem("skew", seed=11, G=8, M_total=3000, OUT_M=240, OUT_N=256)
+    assert p.lhs_scale.numel() == 8
+    _check(p, _run(p, "tcgen05"), label="per-group/tc")
+    _check(p, _run(p, "simt"), label="per-group/simt")
+
+
+def test_launcher_closed_form():
+    """The reference launcher's workload (launcher.cpp:97-112), shrunk: exact known answer."""
+    p = inputs.launcher_problem("gate_up_wgrad", G=8, M_total=8 * 1000 + 5)
+    p = inputs.Problem(**{**p.__dict__, "OUT_M": 480, "OUT_N": 256,
+                          "lhs": p.lhs[:, :480].contiguous(), "rhs": p.rhs[:, :256].contiguous()})
+    out = _run(p, "tcgen05").float().cpu()
+    for g in range(p.G):
+        expect = vo.closed_form_launcher_value(int(p.lens[g]))
+        assert bool((out[g] == expect).all()), (g, out[g].unique()[:4], expect)
+
+
+def test_neighbour_nan_does_not_leak():
+    """Rows of the previous group that the first token block over-reads are zeroed in smem."""
+    p = inputs.make_problem("tiny", seed=13, lens=[100, 50, 200], OUT_M=240, OUT_N=128)
+    lhs = p.lhs.view(torch.uint8).clone()
+    rhs = p.rhs.view(torch.uint8).clone()
+    lhs[:100] = 0x7F  # e4m3fn NaN
+    rhs[:100] = 0x7C  # e5m2 +Inf
+    q = inputs.Problem(**{**p.__dict__, "lhs": lhs.view(torch.float8_e4m3fn),
+                          "rhs": rhs.view(torch.float8_e5m2)})
+    out = _run(q, "tcgen05")
+    assert bool(torch.isnan(out[0].float()).any() or torch.isinf(out[0].float()).any())
+    _check(q, out, groups=[1, 2], label="nan-neighbour")
+
+
+def test_padded_output_strides():
+    p = inputs.make_problem("tiny", seed=17, lens=[333, 0, 444], OUT_M=272, OUT_N=384)
+    big = torch.full((3, 272 + 8, 384 + 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    view = big[:, :272, :384]
+    assert _lib.lib().ggemm_vark_tc_supported(1 << 20, 1 << 20, view.data_ptr(), 272, 384, 272,
+                                              384, view.stride(0), view.stride(1), 1) == 1
+    _run(p, "tcgen05", out=view)
+    _check(p, view, label="padded-C")
+    assert bool((big[:, 272:, :] == 7.0).all()) and bool((big[:, :, 384:] == 7.0).all())
+
+
+def test_unaligned_layout_takes_simt():
+    p = inputs.make_problem("tiny", seed=19, lens=[90, 10, 0, 155], OUT_M=100, OUT_N=72)
+    d = p.to("cuda")
+    wide_l = torch.zeros(255, 101 + 3, dtype=torch.uint8, device="cuda")
+    wide_l[:, 3:103] = d.lhs.view(torch.uint8)
+    lhs_view = wide_l[:, 3:103].view(torch.float8_e4m3fn)  # odd base offset and row pitch 104
+    with pytest.raises(_lib.VarkError) as ei:
+        vark(lhs_view, d.rhs, d.lhs_scale, d.rhs_scale, d.group_offs, path="tcgen05")
+    assert ei.value.code == _lib.ELAYOUT
+    out = vark(lhs_view, d.rhs, d.lhs_scale, d.rhs_scale, d.group_offs)  # auto -> SIMT
+    torch.cuda.synchronize()
+    _check(p, out, label="unaligned")
+
+
+def test_bad_offsets_reported_and_zeroed():
+    p = inputs.make_problem("tiny", seed=23, lens=[64, 64, 64, 64], OUT_M=240, OUT_N=128)
+    d = p.to("cuda")
+    bad = torch.tensor([0, 64, 40, 192, 256], dtype=torch.int64, device="cuda")  # 64 -> 40
+    out = torch.full((4, 240, 128), 3.0, dtype=torch.bfloat16, device="cuda")
+    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, bad, out=out, path="tcgen05")
+    assert _lib.read_status(clear=True) & _lib.DEV_BAD_OFFS
+    assert bool((out[1] == 0).all())
+    past = torch.tensor([0, 64, 128, 192, 257], dtype=torch.int64, device="cuda")  # > m_total
+    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, past, out=out, path="tcgen05")
+    assert _lib.read_status(clear=True) & _lib.DEV_BAD_OFFS
+    assert bool((out[3] == 0).all())
+
+
+def test_fourteen_argument_entry_point():
+    """The drop-in ABI with the reference's argument packing (bench.py:370-385)."""
+    p = inputs.make_problem("tiny", seed=29, lens=[500, 0, 524], OUT_M=480, OUT_N=384)
+    d = p.to("cuda")
+    out = torch.empty(3, 480, 384, dtype=torch.bfloat16, device="cuda")
+    launch_raw(d.lhs.data_ptr(), d.rhs.data_ptr(), out.data_ptr(), d.lhs_scale.data_ptr(),
+               d.rhs_scale.data_ptr(), d.group_offs.data_ptr(), 3, 480, 384, d.lhs.stride(0),
+               d.rhs.stride(0), out.stride(0), out.stride(1), out.stride(2),
+               torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    _check(p, out, label="14-arg")
+
+
+def test_deterministic():
+    p = inputs.make_problem("tiny", seed=31, lens=[1000, 3000, 17], OUT_M=480, OUT_N=640)
+    a = _run(p, "tcgen05")
+    b = _run(p, "tcgen05")
+    assert torch.equal(a, b)
+
+
+@pytest.fixture(scope="module")
+def gate_up_problem():
+    return inputs.make_problem("gate_up", seed=0, device="cuda")
+
+
+def test_gate_up_full_size(gate_up_problem):
+    """BASELINE config 1 at full size: whole-output cosine against the oracle on 4 experts
+    (incl. the smallest and largest), exact scale linearity, and a checksum identity."""
+    p = gate_up_problem
+    out = vark(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
+    torch.cuda.synchronize()
+    assert _lib.read_status(clear=True) == 0
+    groups = sorted({int(np.argmin(p.lens)), int(np.argmax(p.lens)), 0, p.G - 1})
+    cpu = p.to("cpu")
+    _check(cpu, out, groups=groups, label="gate_up")
+    # Linearity: doubling a scale doubles every output exactly (power-of-two scaling).
+    out2 = vark(p.lhs, p.rhs, p.lhs_scale * 2, p.rhs_scale, p.group_offs)
+    torch.cuda.synchronize()
+    assert torch.equal(out2.float(), out.float() * 2)
+    # Checksum: 1^T C_g 1 = sL sR sum_t (sum_m L[t,m]) (sum_n R[t,n]), per group.
+    sl = p.lhs.float().sum(dim=1)
+    sr = p.rhs.float().sum(dim=1)
+    for g in range(0, p.G, 7):
+        lo, hi = int(p.offs[g]), int(p.offs[g + 1])
+        expect = float((sl[lo:hi].double() * sr[lo:hi].double()).sum()) * float(p.lhs_scale) * float(p.rhs_scale)
+        got = float(out[g].double().sum())
+        mag = float((out[g].double().abs()).sum())
+        assert abs(got - expect) <= 1e-3 * mag + 1e-6, (g, got, expect)

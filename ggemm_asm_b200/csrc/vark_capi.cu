@@ -98,11 +98,13 @@ bool tc_layout_ok(const void* lhs, const void* rhs, void* c, int32_t OUT_M, int3
   return true;
 }
 
+// lhs/rhs may be NULL only when the caller states that there are no tokens (m_total == 0):
+// every group is then empty and the operands are never read.
 int check_args(const void* lhs, const void* rhs, void* c, const float* ls, const float* rs,
                const int64_t* offs, int32_t G, int32_t OUT_M, int32_t OUT_N, int32_t slm,
-               int32_t srm, int32_t scg, int32_t scm, int32_t scn) {
-  if (lhs == nullptr || rhs == nullptr || c == nullptr || ls == nullptr || rs == nullptr ||
-      offs == nullptr)
+               int32_t srm, int32_t scg, int32_t scm, int32_t scn, int64_t m_total) {
+  if (m_total != 0 && (lhs == nullptr || rhs == nullptr)) return GGEMM_VARK_EINVAL_PTR;
+  if (c == nullptr || ls == nullptr || rs == nullptr || offs == nullptr)
     return GGEMM_VARK_EINVAL_PTR;
   if (G < 0 || OUT_M <= 0 || OUT_N <= 0) return GGEMM_VARK_EINVAL_SHAPE;
   if (slm < OUT_M || srm < OUT_N) return GGEMM_VARK_EINVAL_STRIDE;
@@ -138,7 +140,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
         const int64_t* offs, int32_t G, int32_t OUT_M, int32_t OUT_N, int32_t slm, int32_t srm,
         int32_t scg, int32_t scm, int32_t scn, int64_t m_total, int32_t scale_stride,
         int32_t path, void* status, uint64_t timeout_ns, void* stream) {
-  int rc = check_args(lhs, rhs, c, ls, rs, offs, G, OUT_M, OUT_N, slm, srm, scg, scm, scn);
+  int rc = check_args(lhs, rhs, c, ls, rs, offs, G, OUT_M, OUT_N, slm, srm, scg, scm, scn,
+                      m_total);
   if (rc != GGEMM_VARK_OK) return rc;
   if (scale_stride != 0 && scale_stride != 1) return GGEMM_VARK_EINVAL_ARG;
   if (path < GGEMM_VARK_PATH_AUTO || path > GGEMM_VARK_PATH_SIMT) return GGEMM_VARK_EINVAL_ARG;
@@ -191,10 +194,14 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   if (tiles > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
 
   CUtensorMap map_rhs, map_lhs, map_c;
-  const uint64_t token_dim = static_cast<uint64_t>(token_limit);
-  if (encode_2d_u8(&map_rhs, rhs, static_cast<uint64_t>(OUT_N), token_dim,
+  // With no tokens the operand maps are never used for a load; they only need to be valid
+  // descriptors, so they point at C.
+  const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
+  const void* lhs_map_base = lhs != nullptr ? lhs : c;
+  const void* rhs_map_base = rhs != nullptr ? rhs : c;
+  if (encode_2d_u8(&map_rhs, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
                    static_cast<uint64_t>(srm)) != CUDA_SUCCESS ||
-      encode_2d_u8(&map_lhs, lhs, static_cast<uint64_t>(OUT_M), token_dim,
+      encode_2d_u8(&map_lhs, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
                    static_cast<uint64_t>(slm)) != CUDA_SUCCESS ||
       encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm) != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;

@@ -86,7 +86,8 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* 
  *
  *  m_total       rows allocated in LHS/RHS, or -1 if unknown. When known, group offsets past
  *                m_total are reported (GGEMM_VARK_DEV_BAD_OFFS) and such groups are written
- *                as zeros instead of being read.
+ *                as zeros instead of being read. With m_total == 0, lhs and rhs may be NULL
+ *                (every group is empty and C is zeroed).
  *  scale_stride  0: lhs_scale/rhs_scale are single values (the reference's tensorwise scales,
  *                bench.py:266-267); 1: they are arrays of G per-group values.
  *  path          GGEMM_VARK_PATH_* selector.

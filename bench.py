@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="approximate CPU-baseline sample budget")
+    ap.add_argument("--groups", type=int, default=None,
+                    help="override G (smaller cases for profiling; not a bench line)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override M_total (smaller cases for profiling; not a bench line)")
     return ap.parse_args()
 
 
@@ -162,6 +166,10 @@ def build_problem(args, rank, world, device):
     if args.config == "ref_exp":
         lens = inputs.reference_exponential_lens(32, 131072, 42)
         p = inputs.make_problem("gate_up", seed=seed, device=device, lens=lens)
+    elif args.groups is not None or args.tokens is not None:
+        cfg = inputs.CONFIGS[name]
+        p = inputs.make_problem(name, seed=seed, device=device, G=args.groups or cfg["G"],
+                                M_total=args.tokens or cfg["M_total"])
     else:
         p = inputs.make_problem(name, seed=seed, device=device)
     return p, "weak"

@@ -23,6 +23,10 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 constexpr int64_t kTokenCoordLimit = INT32_MAX;        // TMA coordinates are int32
+// SM identifiers (%smid) the tensor-map ring covers; %smid is below the SM count on B200 but
+// the PTX ISA does not promise contiguity, so the ring is sized generously (512 KiB).
+constexpr int kTmapSmIds = 256;
+constexpr size_t kStatusBytes = 4096;  // status words, then the 128-byte aligned ring
 
 thread_local int t_last_cuda_error = 0;
 
@@ -30,7 +34,8 @@ struct DeviceState {
   bool ready = false;
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  uint32_t* status = nullptr;  // 256-byte block owned by the library
+  uint32_t* status = nullptr;    // status block owned by the library
+  uint8_t* tmap_ring = nullptr;  // per-SM ring of device-built tensor maps
 };
 
 std::mutex g_mutex;
@@ -63,13 +68,16 @@ int get_device(DeviceState** out, int* dev_out) {
       return fail_cuda(e);
     if (s.cc_major != 10 || s.cc_minor != 0) return GGEMM_VARK_ENO_DEVICE;  // sm_100 only
     if ((e = vark::tc_set_attributes()) != cudaSuccess) return fail_cuda(e);
+    // One allocation per device, kept until exit: the status block and the tensor-map ring.
     void* blk = nullptr;
-    if ((e = cudaMalloc(&blk, 256)) != cudaSuccess) return fail_cuda(e);
-    if ((e = cudaMemset(blk, 0, 256)) != cudaSuccess) {
+    const size_t bytes = kStatusBytes + vark::tc_tmap_ring_bytes(kTmapSmIds);
+    if ((e = cudaMalloc(&blk, bytes)) != cudaSuccess) return fail_cuda(e);
+    if ((e = cudaMemset(blk, 0, bytes)) != cudaSuccess) {
       cudaFree(blk);
       return fail_cuda(e);
     }
     s.status = static_cast<uint32_t*>(blk);
+    s.tmap_ring = static_cast<uint8_t*>(blk) + kStatusBytes;
     if (g_encode == nullptr) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -219,6 +227,12 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.token_limit = token_limit;
   tp.status = st;
   tp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
+  tp.lhs = static_cast<const uint8_t*>(lhs);
+  tp.rhs = static_cast<const uint8_t*>(rhs);
+  tp.stride_lhs = slm;
+  tp.stride_rhs = srm;
+  tp.tmap_ring = dev->tmap_ring;
+  tp.num_sms = kTmapSmIds;
   const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
   cudaError_t e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);
   return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);

@@ -10,11 +10,21 @@ namespace vark {
 // Tile geometry of the tcgen05 path. One output tile is TILE_COLS columns of C (along OUT_N;
 // the MMA M dimension) by TILE_ROWS rows of C (along OUT_M; the MMA N dimension); the token
 // (reduction) dimension is consumed TILE_TOKENS rows per pipeline stage.
+#ifndef VARK_TILE_TOKENS
+#define VARK_TILE_TOKENS 128
+#endif
+#ifndef VARK_STAGES
+#define VARK_STAGES 4
+#endif
 constexpr int TILE_COLS = 128;
 constexpr int TILE_ROWS = 240;
-constexpr int TILE_TOKENS = 128;
-constexpr int STAGES = 4;
+constexpr int TILE_TOKENS = VARK_TILE_TOKENS;  // 64 or 128 (a multiple of the MMA K of 32)
+constexpr int STAGES = VARK_STAGES;
 constexpr int LHS_BOXES = (TILE_ROWS + 127) / 128;  // 128-wide TMA boxes per LHS stage
+
+// Per-SM ring of device-built tensor-map pairs (RHS, LHS) for the group being loaded.
+constexpr int TMAP_SLOTS = 8;
+constexpr int TMAP_PAIR_BYTES = 256;
 
 // Per-warp C staging box of the epilogue (columns x rows), written with one TMA store.
 constexpr int EPI_BOX_COLS = 32;
@@ -33,7 +43,18 @@ struct TcParams {
   int64_t token_limit;   // group offsets above this are invalid
   uint32_t* status;      // device status block (bit flags in word 0)
   uint64_t timeout_ns;   // limit on one pipeline wait
+  const uint8_t* lhs;    // operand bases (per-group tensor maps point inside them)
+  const uint8_t* rhs;
+  int64_t stride_lhs;    // row pitches in bytes
+  int64_t stride_rhs;
+  uint8_t* tmap_ring;    // num_SMs * TMAP_SLOTS * TMAP_PAIR_BYTES bytes, 128-byte aligned
+  int32_t num_sms;       // SM count the ring was sized for
 };
+
+// Bytes of tensor-map ring the tcgen05 kernel needs on a device with `num_sms` SMs.
+inline size_t tc_tmap_ring_bytes(int num_sms) {
+  return static_cast<size_t>(num_sms) * TMAP_SLOTS * TMAP_PAIR_BYTES;
+}
 
 // Dynamic shared memory the tcgen05 kernel needs (bytes, including alignment slack).
 size_t tc_smem_bytes();

@@ -121,6 +121,47 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Device-side tensor-map edits (a map is a 128-byte, 128-byte aligned object)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t id;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
+  return id;
+}
+
+__device__ __forceinline__ void tmap_set_address(uint32_t smem_map, uint64_t global_address) {
+  asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
+                   smem_map),
+               "l"(global_address)
+               : "memory");
+}
+
+template <int ORD>
+__device__ __forceinline__ void tmap_set_dim(uint32_t smem_map, uint32_t extent) {
+  asm volatile("tensormap.replace.tile.global_dim.shared::cta.b1024.b32 [%0], %1, %2;" ::"r"(
+                   smem_map),
+               "n"(ORD), "r"(extent)
+               : "memory");
+}
+
+// Warp-collective: copy a map from shared to global memory and release it to the tensor-map
+// proxy.
+__device__ __forceinline__ void tmap_publish(void* gmem_map, uint32_t smem_map) {
+  asm volatile(
+      "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned"
+      " [%0], [%1], 128;" ::"l"(reinterpret_cast<uint64_t>(gmem_map)),
+      "r"(smem_map)
+      : "memory");
+}
+
+// Acquire a published map before this thread's first TMA that uses it.
+__device__ __forceinline__ void tmap_acquire(const void* gmem_map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
+                   reinterpret_cast<uint64_t>(gmem_map))
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
 // tcgen05 (5th-gen tensor core, tensor memory)
 // ---------------------------------------------------------------------------------------------
 // Whole warp: allocate `ncols` TMEM columns; the base address is written to shared memory.

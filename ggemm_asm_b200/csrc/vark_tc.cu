@@ -21,13 +21,14 @@
 // The epilogue of one tile overlaps the MMAs of the next through the two accumulators.
 //
 // Variable K. A group's tokens [off_g, off_{g+1}) are walked in blocks of 128 that are aligned
-// to the END of the group: block b covers [e - 128*(nkb-b), e - 128*(nkb-b-1)), e = off_{g+1}.
-// Only block 0 can start before off_g; its J = 128*nkb - K leading rows belong to the previous
-// group (or lie at negative coordinates, which TMA fills with zeros). The MMA skips the J/32
-// whole 32-token sub-blocks among them and zeroes the remaining J%32 rows of both operands in
-// shared memory, so a neighbour's data (even Inf/NaN) never enters the sum. No load ever
-// reaches past off_{g+1}, so the kernel needs no token count to stay inside the allocation.
-// Empty groups skip the pipeline entirely: the epilogue TMA-stores zeros for their tiles.
+// to the END of the group, so only block 0 can be partial. Loads go through per-group tensor
+// maps built on the device: the producer copies the host-encoded maps into shared memory,
+// points them at row off_g with a token extent of K_g (tensormap.replace), and publishes them
+// to a per-SM ring in global memory. Block 0 then starts at the negative token coordinate
+// K_g - 128*nkb, and TMA fills the rows outside [0, K_g) with zeros without reading memory:
+// a neighbour's data (even Inf/NaN) never enters the sum, no load reaches past off_{g+1}, and
+// every stage is a uniform 4 MMAs (stages with fewer MMAs stall the recycled-stage pipeline
+// on this hardware). Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA sets the abort
 // flag and GGEMM_VARK_DEV_TIMEOUT in the status block, every role leaves its loop, in-flight
@@ -45,9 +46,9 @@ constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARP0 = 2;
 constexpr int EPI_WARPS = 4;
 
-constexpr uint32_t RHS_STAGE_BYTES = TILE_COLS * TILE_TOKENS;      // 16 KiB
-constexpr uint32_t LHS_BOX_BYTES = 128 * TILE_TOKENS;              // 16 KiB
-constexpr uint32_t LHS_STAGE_BYTES = LHS_BOXES * LHS_BOX_BYTES;    // 32 KiB
+constexpr uint32_t RHS_STAGE_BYTES = TILE_COLS * TILE_TOKENS;      // 16 KiB at 128 tokens
+constexpr uint32_t LHS_BOX_BYTES = 128 * TILE_TOKENS;              // 16 KiB at 128 tokens
+constexpr uint32_t LHS_STAGE_BYTES = LHS_BOXES * LHS_BOX_BYTES;    // 32 KiB at 128 tokens
 constexpr uint32_t STAGE_TX_BYTES = RHS_STAGE_BYTES + LHS_STAGE_BYTES;
 constexpr uint32_t ACC_STRIDE_COLS = 256;
 constexpr uint32_t TMEM_COLS = 512;
@@ -55,7 +56,7 @@ constexpr uint32_t EPI_BUF_BYTES = EPI_BOX_COLS * EPI_BOX_ROWS * 2;  // 1 KiB
 
 static_assert(TILE_COLS == 128, "MMA M is 128 (one CTA, TMEM lane == tile column)");
 static_assert(TILE_ROWS % 16 == 0 && TILE_ROWS <= 256, "MMA N must be a multiple of 16, <= 256");
-static_assert(TILE_TOKENS == 128, "one 128-token block = 4 MMAs of K=32");
+static_assert(TILE_TOKENS == 64 || TILE_TOKENS == 128, "a token block is 2 or 4 MMAs of K=32");
 static_assert(TILE_ROWS <= ACC_STRIDE_COLS, "accumulators must not overlap");
 static_assert(EPI_BOX_COLS == 32, "one epilogue warp covers 32 TMEM lanes");
 
@@ -64,12 +65,14 @@ constexpr uint32_t OFF_RHS = 0;
 constexpr uint32_t OFF_LHS = OFF_RHS + STAGES * RHS_STAGE_BYTES;
 constexpr uint32_t OFF_EPI = OFF_LHS + STAGES * LHS_STAGE_BYTES;
 constexpr uint32_t OFF_ZERO = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t OFF_BARS = OFF_ZERO + EPI_BUF_BYTES;
+constexpr uint32_t OFF_TMAP = OFF_ZERO + EPI_BUF_BYTES;             // 2 x 128 B, 128-aligned
+constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
 constexpr uint32_t NUM_BARS = 2 * STAGES + 2 + 2 + 1;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
 constexpr uint32_t SMEM_USED = OFF_MISC + 16;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;  // alignment slack
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
+static_assert(OFF_TMAP % 128 == 0, "tensor maps must be 128-byte aligned");
 
 constexpr uint32_t IDESC = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
                                         /*A MN-major*/ 1, /*B MN-major*/ 1, 128, TILE_ROWS);
@@ -80,35 +83,32 @@ struct Ctl {
   uint64_t timeout_ns;
 };
 
-// Bounded wait on an mbarrier phase; called by ONE thread.
-__device__ __noinline__ bool wait_bounded(const Ctl& ctl, uint32_t bar, uint32_t parity,
-                                          uint32_t where) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*ctl.abort) return false;
-    if (globaltimer_ns() - t0 > ctl.timeout_ns) {
-      *ctl.abort = 1;
-      if (ctl.status != nullptr) {
-        atomicOr(ctl.status, GGEMM_VARK_DEV_TIMEOUT);
-        atomicExch(ctl.status + 1, where);
-      }
-      return false;
-    }
+// Record a wait that exceeded its limit: stop every role of this CTA and flag the host.
+__device__ __noinline__ void report_timeout(const Ctl& ctl, uint32_t where) {
+  *ctl.abort = 1;
+  if (ctl.status != nullptr) {
+    atomicOr(ctl.status, GGEMM_VARK_DEV_TIMEOUT);
+    atomicExch(ctl.status + 1, where);
   }
 }
 
-// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast to the warp.
+// Bounded wait on an mbarrier phase, executed by every lane of a warp (inline: the waits sit on
+// the critical path between the TMA, MMA and epilogue warps). Returns a warp-uniform verdict:
+// false if the limit expired in any lane or another role already aborted.
 __device__ __forceinline__ bool warp_wait(const Ctl& ctl, uint32_t bar, uint32_t parity,
-                                          uint32_t where, int lane) {
-  int ok = 0;
-  if (lane == 0) ok = wait_bounded(ctl, bar, parity, where) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
+                                          uint32_t where) {
+  bool ok = mbar_try_wait(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!(ok = mbar_try_wait(bar, parity))) {
+      if (*ctl.abort) break;
+      if (globaltimer_ns() - t0 > ctl.timeout_ns) {
+        report_timeout(ctl, where);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
 }
 
 struct TileInfo {
@@ -175,8 +175,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(bar_drain, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&map_rhs);
-    tma_prefetch_desc(&map_lhs);
     tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
@@ -194,30 +192,65 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ======================= TMA producer (lane 0 issues; the warp stays converged) ==========
     const uint64_t policy = l2_policy_evict_last();
+    const uint32_t smid = sm_id();
+    const uint32_t smem_maps = base + OFF_TMAP;
     uint32_t stage = 0, phase = 0;
     uint32_t used_mask = 0, parity_mask = 0;  // per stage: issued at least once / last parity
-    bool ok = true;
+    int cur_group = -1;
+    uint32_t slot = 0;
+    const CUtensorMap* gmap_rhs = nullptr;
+    const CUtensorMap* gmap_lhs = nullptr;
+    bool ok = smid < static_cast<uint32_t>(p.num_sms);
+    if (!ok && lane == 0) report_timeout(ctl, 0x500u);  // ring too small: refuse to run
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const TileInfo t = decode_tile(p, tile, false);
       if (t.tokens == 0) continue;
+      if (t.g != cur_group) {
+        // Per-group maps: base at row off_g, token extent K_g, into the next ring slot.
+        slot = (slot + 1) % TMAP_SLOTS;
+        uint8_t* const pair =
+            p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
+        if (lane < 16) {
+          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_rhs : &map_lhs);
+          reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
+        }
+        __syncwarp();
+        if (lane == 0) {
+          const int64_t lo = t.end - t.tokens;
+          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
+          tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
+          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
+          tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
+        }
+        __syncwarp();
+        tmap_publish(pair, smem_maps);
+        tmap_publish(pair + 128, smem_maps + 128);
+        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair);
+        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
+        if (lane == 0) {
+          tmap_acquire(gmap_rhs);
+          tmap_acquire(gmap_lhs);
+        }
+        __syncwarp();
+        cur_group = t.g;
+      }
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
-      const int64_t first = t.end - static_cast<int64_t>(TILE_TOKENS) * nkb;
+      const int32_t y0 = t.tokens - TILE_TOKENS * nkb;  // <= 0: rows before the group read as 0
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage, lane)) {
+        if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
           ok = false;
           break;
         }
         if (lane == 0) {
           const uint32_t fb = bar_full + 8 * stage;
           mbar_arrive_expect_tx(fb, STAGE_TX_BYTES);
-          const int32_t y =
-              static_cast<int32_t>(first + static_cast<int64_t>(TILE_TOKENS) * kb);
-          tma_load_2d_hint(base + OFF_RHS + stage * RHS_STAGE_BYTES, &map_rhs, fb, t.col0, y,
+          const int32_t y = y0 + TILE_TOKENS * kb;
+          tma_load_2d_hint(base + OFF_RHS + stage * RHS_STAGE_BYTES, gmap_rhs, fb, t.col0, y,
                            policy);
 #pragma unroll
           for (int b = 0; b < LHS_BOXES; ++b)
             tma_load_2d_hint(base + OFF_LHS + stage * LHS_STAGE_BYTES + b * LHS_BOX_BYTES,
-                             &map_lhs, fb, t.row0 + 128 * b, y, policy);
+                             gmap_lhs, fb, t.row0 + 128 * b, y, policy);
         }
         __syncwarp();
         used_mask |= 1u << stage;
@@ -250,46 +283,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const TileInfo t = decode_tile(p, tile, false);
       if (t.tokens == 0) continue;
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
-      const int junk = TILE_TOKENS * nkb - t.tokens;  // leading rows of block 0 not in group
-      if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc, lane)) break;
+      if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
       tc_fence_after_sync();
       const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE_COLS;
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage, lane)) {
+        if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         const uint32_t a_stage = base + OFF_RHS + stage * RHS_STAGE_BYTES;
         const uint32_t b_stage = base + OFF_LHS + stage * LHS_STAGE_BYTES;
-        int k_first = 0;
-        if (kb == 0 && junk > 0) {
-          k_first = junk >> 5;
-          const int z0 = k_first * 32, z1 = junk;
-          if (z1 > z0) {
-            // Zero rows [z0, z1) of every box of this stage (row = 128 contiguous bytes; the
-            // 128B swizzle only permutes 16-byte chunks inside a row).
-            const int per_box = (z1 - z0) * 8;
-            const int total = per_box * (1 + LHS_BOXES);
-            for (int i = lane; i < total; i += 32) {
-              const int box = i / per_box;
-              const int rem = i - box * per_box;
-              const uint32_t box_base =
-                  box == 0 ? a_stage : b_stage + static_cast<uint32_t>(box - 1) * LHS_BOX_BYTES;
-              const uint32_t addr = box_base + static_cast<uint32_t>(z0 + (rem >> 3)) * 128u +
-                                    static_cast<uint32_t>(rem & 7) * 16u;
-              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u)
-                           : "memory");
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-          }
-        }
         if (lane == 0) {
-          for (int ks = k_first; ks < TILE_TOKENS / 32; ++ks) {
+#pragma unroll
+          for (int ks = 0; ks < TILE_TOKENS / 32; ++ks) {
             const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, RHS_STAGE_BYTES, 1024u);
             const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, LHS_BOX_BYTES, 1024u);
-            mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > k_first) ? 1u : 0u);
+            mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(bar_empty + 8 * stage);  // frees the stage once these MMAs finish
         }
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const float scale = __ldg(p.lhs_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
                           __ldg(p.rhs_scale + static_cast<int64_t>(t.g) * p.scale_stride);
-      if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc, lane)) break;
+      if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
       if (col_live) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_STRIDE_COLS;

@@ -28,6 +28,7 @@ DEV_TIMEOUT = 0x2
 PATH_AUTO = 0
 PATH_TCGEN05 = 1
 PATH_SIMT = 2
+PATH_TCGEN05_1SM = 3
 
 # Every function the header declares, with its ctypes signature.
 _vp = ctypes.c_void_p

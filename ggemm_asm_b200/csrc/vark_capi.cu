@@ -68,6 +68,7 @@ int get_device(DeviceState** out, int* dev_out) {
       return fail_cuda(e);
     if (s.cc_major != 10 || s.cc_minor != 0) return GGEMM_VARK_ENO_DEVICE;  // sm_100 only
     if ((e = vark::tc_set_attributes()) != cudaSuccess) return fail_cuda(e);
+    if ((e = vark::tc2_set_attributes()) != cudaSuccess) return fail_cuda(e);
     // One allocation per device, kept until exit: the status block and the tensor-map ring.
     void* blk = nullptr;
     const size_t bytes = kStatusBytes + vark::tc_tmap_ring_bytes(kTmapSmIds);
@@ -131,17 +132,19 @@ CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// C as a 3-D bf16 tensor {OUT_N, OUT_M, G}; the box and swizzle follow the kernel's epilogue.
 CUresult encode_c(CUtensorMap* map, void* c, int32_t G, int32_t OUT_M, int32_t OUT_N,
-                  int32_t scg, int32_t scm) {
+                  int32_t scg, int32_t scm, uint32_t box_cols, uint32_t box_rows,
+                  CUtensorMapSwizzle swizzle) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OUT_N), static_cast<cuuint64_t>(OUT_M),
                               static_cast<cuuint64_t>(G)};
   const cuuint64_t strides[2] = {2ull * static_cast<cuuint64_t>(scm),
                                  2ull * static_cast<cuuint64_t>(scg)};
-  const cuuint32_t box[3] = {vark::EPI_BOX_COLS, vark::EPI_BOX_ROWS, 1};
+  const cuuint32_t box[3] = {box_cols, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
 int run(const void* lhs, const void* rhs, void* c, const float* ls, const float* rs,
@@ -152,7 +155,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
                       m_total);
   if (rc != GGEMM_VARK_OK) return rc;
   if (scale_stride != 0 && scale_stride != 1) return GGEMM_VARK_EINVAL_ARG;
-  if (path < GGEMM_VARK_PATH_AUTO || path > GGEMM_VARK_PATH_SIMT) return GGEMM_VARK_EINVAL_ARG;
+  if (path < GGEMM_VARK_PATH_AUTO || path > GGEMM_VARK_PATH_TCGEN05_1SM)
+    return GGEMM_VARK_EINVAL_ARG;
   if (m_total < -1) return GGEMM_VARK_EINVAL_ARG;
   if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
   if (G == 0) return GGEMM_VARK_OK;
@@ -168,7 +172,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
 
   const bool tc_ok = tc_layout_ok(lhs, rhs, c, OUT_M, OUT_N, slm, srm, scg, scm, scn);
   bool use_tc = tc_ok;
-  if (path == GGEMM_VARK_PATH_TCGEN05 && !tc_ok) return GGEMM_VARK_ELAYOUT;
+  if ((path == GGEMM_VARK_PATH_TCGEN05 || path == GGEMM_VARK_PATH_TCGEN05_1SM) && !tc_ok)
+    return GGEMM_VARK_ELAYOUT;
   if (path == GGEMM_VARK_PATH_SIMT) use_tc = false;
 
   if (!use_tc) {
@@ -195,9 +200,12 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
     return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
   }
 
-  // Tensor-core path.
-  const int32_t row_tiles = (OUT_M + vark::TILE_ROWS - 1) / vark::TILE_ROWS;
-  const int32_t col_tiles = (OUT_N + vark::TILE_COLS - 1) / vark::TILE_COLS;
+  // Tensor-core paths.
+  const bool pair = path != GGEMM_VARK_PATH_TCGEN05_1SM && dev->sm_count >= 2;
+  const int32_t rt = pair ? 2 * vark::PAIR_HALF : vark::TILE_ROWS;
+  const int32_t ct = pair ? vark::PAIR_COLS : vark::TILE_COLS;
+  const int32_t row_tiles = (OUT_M + rt - 1) / rt;
+  const int32_t col_tiles = (OUT_N + ct - 1) / ct;
   const int64_t tiles = static_cast<int64_t>(G) * row_tiles * col_tiles;
   if (tiles > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
 
@@ -207,11 +215,15 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
   const void* lhs_map_base = lhs != nullptr ? lhs : c;
   const void* rhs_map_base = rhs != nullptr ? rhs : c;
+  const CUresult enc_c =
+      pair ? encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+           : encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, vark::EPI_BOX_COLS,
+                      vark::EPI_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (encode_2d_u8(&map_rhs, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
                    static_cast<uint64_t>(srm)) != CUDA_SUCCESS ||
       encode_2d_u8(&map_lhs, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
                    static_cast<uint64_t>(slm)) != CUDA_SUCCESS ||
-      encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm) != CUDA_SUCCESS)
+      enc_c != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
 
   vark::TcParams tp;
@@ -233,8 +245,14 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.stride_rhs = srm;
   tp.tmap_ring = dev->tmap_ring;
   tp.num_sms = kTmapSmIds;
-  const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
-  cudaError_t e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);
+  cudaError_t e;
+  if (pair) {
+    const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;
+    e = vark::tc2_launch(map_lhs, map_rhs, map_c, tp, static_cast<int>(2 * clusters), s);
+  } else {
+    const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
+    e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);
+  }
   return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
 }
 

@@ -22,6 +22,15 @@ constexpr int TILE_TOKENS = VARK_TILE_TOKENS;  // 64 or 128 (a multiple of the M
 constexpr int STAGES = VARK_STAGES;
 constexpr int LHS_BOXES = (TILE_ROWS + 127) / 128;  // 128-wide TMA boxes per LHS stage
 
+// Geometry of the CTA-pair (cta_group::2) kernel: a work item is 256 C rows (128 per CTA) by
+// 256 C columns; 128 tokens per pipeline stage.
+#ifndef VARK_PAIR_STAGES
+#define VARK_PAIR_STAGES 6
+#endif
+constexpr int PAIR_HALF = 128;
+constexpr int PAIR_COLS = 256;
+constexpr int PAIR_STAGES = VARK_PAIR_STAGES;
+
 // Per-SM ring of device-built tensor-map pairs (RHS, LHS) for the group being loaded.
 constexpr int TMAP_SLOTS = 8;
 constexpr int TMAP_PAIR_BYTES = 256;
@@ -38,8 +47,8 @@ struct TcParams {
   int32_t G;
   int32_t OUT_M;
   int32_t OUT_N;
-  int32_t row_tiles;     // ceil(OUT_M / TILE_ROWS)
-  int32_t col_tiles;     // ceil(OUT_N / TILE_COLS)
+  int32_t row_tiles;     // number of row (OUT_M) tiles of the launched kernel's geometry
+  int32_t col_tiles;     // number of column (OUT_N) tiles
   int64_t token_limit;   // group offsets above this are invalid
   uint32_t* status;      // device status block (bit flags in word 0)
   uint64_t timeout_ns;   // limit on one pipeline wait
@@ -82,5 +91,13 @@ cudaError_t simt_launch(const SimtParams& p, cudaStream_t stream);
 
 // Raise the tcgen05 kernel's dynamic shared-memory limit (once per device).
 cudaError_t tc_set_attributes();
+
+// CTA-pair kernel (vark_tc2.cu): same parameters; row_tiles/col_tiles count 256-wide tiles and
+// `grid` must be even (one cluster of two CTAs per pair of SMs).
+size_t tc2_smem_bytes();
+cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
+                       const CUtensorMap& map_c, const TcParams& p, int grid,
+                       cudaStream_t stream);
+cudaError_t tc2_set_attributes();
 
 }  // namespace vark

@@ -1,0 +1,437 @@
+// vark_tc2.cu - persistent sm_100a tcgen05 kernel for the variable-K grouped FP8 wgrad on CTA
+// pairs (cta_group::2). This is the default tensor-core path.
+//
+// Computes, for every group g, C[g] = sL*sR * LHS[off_g:off_{g+1}]^T . RHS[off_g:off_{g+1}]
+// (ggemm-asm README.md:5,45-48; bench.py:182-193 "dW = lhs^T @ rhs" per expert).
+//
+// Tile and operands. One work item is (group g, 256 rows of C, 256 columns of C) and is computed
+// by a cluster of two CTAs with one tcgen05.mma.cta_group::2 (M=256, N=256, K=32) per 32 tokens:
+//   * MMA-M runs along OUT_M (C rows): operand A = LHS (e4m3). CTA r of the pair holds rows
+//     [m0 + 128r, m0 + 128r + 128) of the tile and its TMEM accumulates those 128 C rows.
+//   * MMA-N runs along OUT_N (C columns): operand B = RHS (e5m2). CTA r holds columns
+//     [n0 + 128r, n0 + 128r + 128); the MMA reads both halves across the pair.
+// Both operands stay in their token-major layout, which for the MMA is MN-major: a TMA box of
+// 128 contiguous features x 128 tokens lands with the 128-byte swizzle of the canonical
+// MN-major layout. Per CTA and 128 tokens that is 32 KiB (16 KiB of each operand) for
+// 128x256x128 MACs, two thirds of the bytes per MAC of a single-CTA 128x240 tile; the kernel is
+// bound by how fast one SM can ingest TMA data from L2, so bytes per MAC set the speed.
+// Shapes that are not multiples of 256 (2880 = 11.25 x 256, 5760 = 22.5 x 256) get boxes that
+// run past the tensor edge: TMA fills them with zeros without reading memory and the epilogue's
+// TMA store clips them, so only tensor-core time is spent on them.
+//
+// Warp roles (192 threads per CTA, one CTA per SM, 74 pairs on 148 SMs, persistent over a
+// static round-robin schedule of work items by cluster):
+//   warp 0      TMA producer (both CTAs): 6-stage ring of {LHS 128x128, RHS 128x128} blocks,
+//               completion counted on the pair leader's full barrier
+//   warp 1      TMEM owner (both CTAs, cta_group::2 allocation of all 512 columns = two
+//               128x256 fp32 accumulators); in the leader also the MMA issuer
+//   warps 2..5  epilogue (both CTAs): tcgen05.ld 32 columns -> * (sL*sR) -> bf16 (RNE) ->
+//               64B-swizzled smem box (32x32) -> TMA store; warp w owns TMEM lanes
+//               32*(w%4)..+31 = 32 rows of this CTA's half of the tile
+// The leader's commits arrive on both CTAs' barriers (tcgen05.commit multicast); the epilogue
+// warps of both CTAs release an accumulator on the leader's barrier.
+//
+// Variable K. As in the single-CTA kernel (vark_tc.cu): token blocks of 128 aligned to the END
+// of the group, loads through per-group tensor maps built on the device (base at row off_g,
+// token extent K_g), so the partial first block starts at a negative coordinate and TMA fills
+// the rows before the group with zeros; every stage is a uniform 4 MMAs. Empty groups skip the
+// pipeline and the epilogue stores zeros.
+//
+// Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
+// GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs of the pair, every role leaves its
+// loop, in-flight loads and MMAs are drained with bounded waits, and the pair meets at a
+// cluster barrier before TMEM is freed.
+#include <cuda_bf16.h>
+
+#include "../../include/ggemm_vark.h"
+#include "vark_internal.h"
+#include "vark_ptx.cuh"
+
+namespace vark {
+namespace {
+
+constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARP0 = 2;
+constexpr int EPI_WARPS = 4;
+constexpr int PAIR_ROWS = 2 * PAIR_HALF;   // C rows per work item (MMA M)
+constexpr int TILE_N2 = PAIR_COLS;         // C columns per work item (MMA N)
+constexpr int TK = 128;                    // tokens per stage
+constexpr int ST = PAIR_STAGES;
+
+constexpr uint32_t BOX_BYTES = 128 * TK;                 // 16 KiB per operand box
+constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;          // LHS box + RHS box
+constexpr uint32_t ACC_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int EPI_COLS = 32;                             // C columns per epilogue box
+constexpr int EPI_ROWS = 32;                             // C rows per epilogue box (one warp)
+constexpr uint32_t EPI_BUF_BYTES = EPI_COLS * EPI_ROWS * 2;  // 2 KiB
+
+static_assert(PAIR_HALF == 128 && PAIR_COLS == 256, "pair tile is 256 x 256");
+
+// Shared-memory map (offsets from a 1024-byte aligned base; identical in both CTAs).
+constexpr uint32_t OFF_LHS = 0;
+constexpr uint32_t OFF_RHS = OFF_LHS + ST * BOX_BYTES;
+constexpr uint32_t OFF_EPI = OFF_RHS + ST * BOX_BYTES;
+constexpr uint32_t OFF_ZERO = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
+constexpr uint32_t OFF_TMAP = OFF_ZERO + EPI_BUF_BYTES;
+constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
+constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1;
+constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
+constexpr uint32_t SMEM_USED = OFF_MISC + 16;
+constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
+static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
+static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0, "alignment");
+
+constexpr uint32_t IDESC = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
+                                        /*A MN-major*/ 1, /*B MN-major*/ 1, PAIR_ROWS, TILE_N2);
+
+struct Ctl {
+  volatile int* abort;
+  uint32_t peer_abort;  // shared::cluster address of the peer CTA's abort flag
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+
+__device__ __noinline__ void report_timeout(const Ctl& ctl, uint32_t where) {
+  *ctl.abort = 1;
+  st_shared_cluster_u32(ctl.peer_abort, 1u);
+  if (ctl.status != nullptr) {
+    atomicOr(ctl.status, GGEMM_VARK_DEV_TIMEOUT);
+    atomicExch(ctl.status + 1, where);
+  }
+}
+
+// Bounded wait by every lane of a warp; warp-uniform verdict (see vark_tc.cu).
+__device__ __forceinline__ bool warp_wait(const Ctl& ctl, uint32_t bar, uint32_t parity,
+                                          uint32_t where) {
+  bool ok = mbar_try_wait(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!(ok = mbar_try_wait(bar, parity))) {
+      if (*ctl.abort) break;
+      if (globaltimer_ns() - t0 > ctl.timeout_ns) {
+        report_timeout(ctl, where);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+struct Item {
+  int g, m0, n0;   // group, first C row, first C column of the pair tile
+  int tokens;      // K_g (0 for empty or invalid groups)
+  int64_t end;     // off_{g+1}
+};
+
+__device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool report) {
+  const int per_group = p.row_tiles * p.col_tiles;
+  Item t;
+  t.g = item / per_group;
+  const int r = item - t.g * per_group;
+  t.n0 = (r % p.col_tiles) * TILE_N2;
+  t.m0 = (r / p.col_tiles) * PAIR_ROWS;
+  const int64_t lo = __ldg(p.group_offs + t.g);
+  const int64_t hi = __ldg(p.group_offs + t.g + 1);
+  if (lo < 0 || hi < lo || hi > p.token_limit) {
+    if (report && p.status != nullptr) atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
+    t.tokens = 0;
+    t.end = 0;
+  } else {
+    t.tokens = static_cast<int>(hi - lo);
+    t.end = hi;
+  }
+  return t;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    vark_tc2_kernel(const __grid_constant__ CUtensorMap map_lhs,
+                    const __grid_constant__ CUtensorMap map_rhs,
+                    const __grid_constant__ CUtensorMap map_c, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* const sbase = smem_raw + (base - raw_addr);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  const uint32_t bar_full = base + OFF_BARS;         // [ST]  used in the leader only
+  const uint32_t bar_empty = bar_full + 8 * ST;      // [ST]  both CTAs
+  const uint32_t bar_tfull = bar_empty + 8 * ST;     // [2]   both CTAs
+  const uint32_t bar_tempty = bar_tfull + 16;        // [2]   used in the leader only
+  const uint32_t bar_drain = bar_tempty + 16;        // [1]   leader
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(sbase + OFF_MISC + 4);
+
+  // ---- set-up -------------------------------------------------------------------------------
+  {
+    uint32_t* z = reinterpret_cast<uint32_t*>(sbase + OFF_ZERO);
+    for (int i = threadIdx.x; i < static_cast<int>(EPI_BUF_BYTES / 4); i += NUM_THREADS) z[i] = 0u;
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(bar_full + 8 * s, 2);   // one expect-tx arrival from each CTA's producer
+      mbar_init(bar_empty + 8 * s, 1);  // the leader's commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);                // the leader's commit
+      mbar_init(bar_tempty + 8 * a, 2 * EPI_WARPS);   // every epilogue warp of the pair
+    }
+    mbar_init(bar_drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&map_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive/commit
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const Ctl ctl{abort_flag, mapa_shared(smem_u32(const_cast<int*>(abort_flag)), rank ^ 1u),
+                p.status, p.timeout_ns};
+  const int num_items = p.G * p.row_tiles * p.col_tiles;
+  const int cluster = static_cast<int>(cluster_id_x());
+  const int nclusters = static_cast<int>(num_clusters_x());
+
+  if (warp == 0) {
+    // ======================= TMA producer (both CTAs) =======================================
+    const uint64_t policy = l2_policy_evict_last();
+    const uint32_t smid = sm_id();
+    const uint32_t smem_maps = base + OFF_TMAP;
+    uint32_t stage = 0, phase = 0;
+    int cur_group = -1;
+    uint32_t slot = 0;
+    const CUtensorMap* gmap_lhs = nullptr;
+    const CUtensorMap* gmap_rhs = nullptr;
+    bool ok = smid < static_cast<uint32_t>(p.num_sms);
+    if (!ok && lane == 0) report_timeout(ctl, 0x500u);
+    for (int item = cluster; item < num_items && ok; item += nclusters) {
+      const Item t = decode_item(p, item, false);
+      if (t.tokens == 0) continue;
+      if (t.g != cur_group) {
+        slot = (slot + 1) % TMAP_SLOTS;
+        uint8_t* const pair =
+            p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
+        if (lane < 16) {
+          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_lhs : &map_rhs);
+          reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
+        }
+        __syncwarp();
+        if (lane == 0) {
+          const int64_t lo = t.end - t.tokens;
+          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
+          tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
+          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
+          tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
+        }
+        __syncwarp();
+        tmap_publish(pair, smem_maps);
+        tmap_publish(pair + 128, smem_maps + 128);
+        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair);
+        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
+        if (lane == 0) {
+          tmap_acquire(gmap_lhs);
+          tmap_acquire(gmap_rhs);
+        }
+        __syncwarp();
+        cur_group = t.g;
+      }
+      const int nkb = (t.tokens + TK - 1) / TK;
+      const int32_t y0 = t.tokens - TK * nkb;  // <= 0: rows before the group read as zeros
+      const int32_t xl = t.m0 + PAIR_HALF * static_cast<int32_t>(rank);
+      const int32_t xr = t.n0 + PAIR_HALF * static_cast<int32_t>(rank);
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
+          mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
+          const int32_t y = y0 + TK * kb;
+          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, gmap_lhs, fb, xl, y, policy);
+          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, gmap_rhs, fb, xr, y, policy);
+        }
+        __syncwarp();
+        if (++stage == ST) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // Loads still in flight are drained through the empty barriers: every stage this producer
+    // filled is released by the leader's commit once its MMAs (which waited for the data)
+    // finish; after an abort the wait is bounded.
+    if (lane == 0) {
+      for (int s = 0; s < ST; ++s) {
+        const uint64_t t0 = globaltimer_ns();
+        // A stage filled k times has had k commits when drained: its parity equals the fill
+        // parity. Waiting for "phase ^ 1" of the CURRENT position covers the stages ahead.
+        const uint32_t par = (static_cast<uint32_t>(s) < stage) ? phase : (phase ^ 1u);
+        while (!mbar_try_wait(bar_empty + 8 * s, par)) {
+          if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ======================= MMA issuer (pair leader only) ==================================
+    if (leader) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int item = cluster; item < num_items && ok; item += nclusters) {
+        const Item t = decode_item(p, item, false);
+        if (t.tokens == 0) continue;
+        const int nkb = (t.tokens + TK - 1) / TK;
+        if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a_stage = base + OFF_LHS + stage * BOX_BYTES;
+          const uint32_t b_stage = base + OFF_RHS + stage * BOX_BYTES;
+          if (lane == 0) {
+#pragma unroll
+            for (int ks = 0; ks < TK / 32; ++ks) {
+              const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
+              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
+              mma_f8f6f4_pair(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+            }
+            mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
+          }
+          __syncwarp();
+          if (++stage == ST) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (lane == 0) mma_commit_pair(bar_tfull + 8 * acc, 0x3);  // accumulator ready
+        __syncwarp();
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (lane == 0) {
+        mma_commit_pair(bar_drain, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_drain, 0)) {
+          if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    // ======================= epilogue (warps 2..5, both CTAs) ===============================
+    const int ew = warp - EPI_WARP0;
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t zero_buf = base + OFF_ZERO;
+    const uint32_t epi_sh = base + OFF_EPI + ew * 2 * EPI_BUF_BYTES;
+    const uint32_t leader_tempty = mapa_shared(bar_tempty, 0);
+    uint32_t acc = 0, acc_phase = 0;
+    uint32_t nstore = 0;
+    for (int item = cluster; item < num_items; item += nclusters) {
+      const Item t = decode_item(p, item, leader && quarter == 0 && lane == 0);
+      const int yrow = t.m0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C row
+      const bool rows_live = yrow < p.OUT_M;
+      const int cols_here = min(TILE_N2, p.OUT_N - t.n0);
+      const int nchunks = (cols_here + EPI_COLS - 1) / EPI_COLS;
+      if (t.tokens == 0) {
+        if (rows_live && lane == 0) {
+          for (int c = 0; c < nchunks; ++c)
+            tma_store_3d(&map_c, zero_buf, t.n0 + c * EPI_COLS, yrow, t.g);
+          bulk_commit_group();
+        }
+        __syncwarp();
+        continue;
+      }
+      const float scale = __ldg(p.lhs_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
+                          __ldg(p.rhs_scale + static_cast<int64_t>(t.g) * p.scale_stride);
+      if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
+      tc_fence_after_sync();
+      if (rows_live) {
+        const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_acc + c * EPI_COLS, r);
+          tmem_ld_wait();
+          const uint32_t buf = epi_sh + (nstore & 1u) * EPI_BUF_BYTES;
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that used `buf` has read it
+          __syncwarp();
+          // Row `lane` of the 32x32 box: 64 bytes = four 16-byte chunks, stored with the
+          // 64-byte swizzle (chunk ^= (row >> 1) & 3) that the C tensor map expects.
+          const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
+          const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const __nv_bfloat162 v = __floats2bfloat162_rn(
+                  __uint_as_float(r[ch * 8 + 2 * k]) * scale,
+                  __uint_as_float(r[ch * 8 + 2 * k + 1]) * scale);
+              w[k] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             row_addr + ((static_cast<uint32_t>(ch) ^ sw) << 4)),
+                         "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, yrow, t.g);
+            bulk_commit_group();
+          }
+          ++nstore;
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty + 8 * acc);
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ---- teardown -----------------------------------------------------------------------------
+  tc_fence_before_sync();
+  cluster_sync_all();  // the leader's MMAs into the peer's TMEM/smem are done
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+size_t tc2_smem_bytes() { return SMEM_ALLOC; }
+
+cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
+                       const CUtensorMap& map_c, const TcParams& p, int grid,
+                       cudaStream_t stream) {
+  vark_tc2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_lhs, map_rhs, map_c, p);
+  return cudaGetLastError();
+}
+
+cudaError_t tc2_set_attributes() {
+  return cudaFuncSetAttribute(vark_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(SMEM_ALLOC));
+}
+
+}  // namespace vark

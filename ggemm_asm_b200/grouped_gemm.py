@@ -16,7 +16,8 @@ from . import _lib
 LHS_DTYPE = torch.float8_e4m3fn
 RHS_DTYPE = torch.float8_e5m2
 
-_PATHS = {"auto": _lib.PATH_AUTO, "tcgen05": _lib.PATH_TCGEN05, "simt": _lib.PATH_SIMT}
+_PATHS = {"auto": _lib.PATH_AUTO, "tcgen05": _lib.PATH_TCGEN05, "simt": _lib.PATH_SIMT,
+          "tcgen05_1sm": _lib.PATH_TCGEN05_1SM}
 
 
 def _check_inputs(lhs, rhs, lhs_scale, rhs_scale, group_offs):
@@ -70,7 +71,8 @@ def grouped_gemm_fp8_tensorwise_variable_k(lhs: torch.Tensor, rhs: torch.Tensor,
     lhs: [M_total, OUT_M] float8_e4m3fn, rhs: [M_total, OUT_N] float8_e5m2 (token-major),
     lhs_scale / rhs_scale: float32 with 1 element (tensorwise, as the reference) or G elements
     (per group), group_offs: int64 [G+1]. ``out`` (optional) is a [G, OUT_M, OUT_N] bf16 tensor
-    with contiguous rows; it is overwritten. ``path`` selects "auto" | "tcgen05" | "simt".
+    with contiguous rows; it is overwritten. ``path`` selects "auto" | "tcgen05" (CTA pairs) |
+    "tcgen05_1sm" (single CTA) | "simt".
     ``status``: optional int32 CUDA tensor of >= 64 elements used as the device status block.
     """
     G, scale_stride = _check_inputs(lhs, rhs, lhs_scale, rhs_scale, group_offs)

@@ -60,8 +60,9 @@ extern "C" {
 
 /* ---- path selection flags for ggemm_vark_fp8_wgrad_ex ------------------------------------ */
 #define GGEMM_VARK_PATH_AUTO      0      /* tensor-core path when the layout allows, else SIMT */
-#define GGEMM_VARK_PATH_TCGEN05   1      /* force the tcgen05 path (ELAYOUT if not expressible) */
+#define GGEMM_VARK_PATH_TCGEN05   1      /* force the tcgen05 CTA-pair path (ELAYOUT if not expressible) */
 #define GGEMM_VARK_PATH_SIMT      2      /* force the CUDA-core path (any strides) */
+#define GGEMM_VARK_PATH_TCGEN05_1SM 3    /* force the single-CTA tcgen05 path (same layout rules) */
 
 /*
  * ggemm_vark_fp8_wgrad - the drop-in for `_grouped_variable_k_gemm_kernel`.

@@ -38,7 +38,7 @@ def test_codes_match_header():
     for name in ["DEV_BAD_OFFS", "DEV_TIMEOUT"]:
         m = re.search(rf"#define GGEMM_VARK_{name}\s+(0x[0-9a-fA-F]+)u", text)
         assert m and int(m.group(1), 16) == getattr(_lib, name), name
-    for name in ["PATH_AUTO", "PATH_TCGEN05", "PATH_SIMT"]:
+    for name in ["PATH_AUTO", "PATH_TCGEN05", "PATH_SIMT", "PATH_TCGEN05_1SM"]:
         m = re.search(rf"#define GGEMM_VARK_{name}\s+(\d+)", text)
         assert m and int(m.group(1)) == getattr(_lib, name), name
 
@@ -85,7 +85,7 @@ def test_bad_shapes_and_strides_rejected(kw, code):
     assert call14(**kw) == code
 
 
-@pytest.mark.parametrize("kw", [dict(scale_stride=2), dict(scale_stride=-1), dict(path=3),
+@pytest.mark.parametrize("kw", [dict(scale_stride=2), dict(scale_stride=-1), dict(path=4),
                                 dict(path=-1), dict(m_total=-2), dict(status=P + 8)])
 def test_bad_extended_args_rejected(kw):
     assert call_ex(**kw) == _lib.EINVAL_ARG

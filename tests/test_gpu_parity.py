@@ -44,7 +44,11 @@ def _run(p, path="auto", out=None):
     return o
 
 
-@pytest.mark.parametrize("path", ["tcgen05", "simt"])
+TC_PATHS = ["tcgen05", "tcgen05_1sm"]
+ALL_PATHS = TC_PATHS + ["simt"]
+
+
+@pytest.mark.parametrize("path", ALL_PATHS)
 def test_tiny_config(path):
     p = inputs.make_problem("tiny", seed=0)
     assert p.offs.tolist() == [0, 256, 256, 768, 1024]
@@ -63,47 +67,51 @@ RAGGED = [
 
 
 @pytest.mark.parametrize("lens", RAGGED, ids=[str(i) for i in range(len(RAGGED))])
-@pytest.mark.parametrize("path", ["tcgen05", "simt"])
+@pytest.mark.parametrize("path", ALL_PATHS)
 def test_ragged_groups(lens, path):
     p = inputs.make_problem("tiny", seed=3, lens=lens, OUT_M=272, OUT_N=384)
     _check(p, _run(p, path), label=f"ragged{lens}/{path}")
 
 
 @pytest.mark.parametrize("shape", [(240, 128), (480, 256), (16, 16), (2880, 128), (64, 5760),
-                                   (496, 400)])
-def test_tile_edges(shape):
+                                   (496, 400), (256, 256), (272, 272), (128, 640)])
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_tile_edges(shape, path):
     OUT_M, OUT_N = shape
     p = inputs.make_problem("tiny", seed=5, lens=[200, 57, 0, 301], OUT_M=OUT_M, OUT_N=OUT_N)
-    _check(p, _run(p, "tcgen05"), label=f"edges{shape}")
+    _check(p, _run(p, path), label=f"edges{shape}/{path}")
 
 
-def test_tc_equals_simt_bitwise_close():
+def test_tc_paths_agree_with_simt():
     p = inputs.make_problem("tiny", seed=7, lens=[700, 1, 300, 2000], OUT_M=480, OUT_N=512)
     a = _run(p, "tcgen05").float()
     b = _run(p, "simt").float()
-    assert vo.cosine(a, b) >= COS_MIN
+    c = _run(p, "tcgen05_1sm").float()
+    assert vo.cosine(a, b) >= COS_MIN and vo.cosine(c, b) >= COS_MIN
 
 
-def test_per_group_scales():
+@pytest.mark.parametrize("path", ALL_PATHS)
+def test_per_group_scales(path):
     p = inputs.make_problem("skew", seed=11, G=8, M_total=3000, OUT_M=240, OUT_N=256)
     assert p.lhs_scale.numel() == 8
-    _check(p, _run(p, "tcgen05"), label="per-group/tc")
-    _check(p, _run(p, "simt"), label="per-group/simt")
+    _check(p, _run(p, path), label=f"per-group/{path}")
 
 
-def test_launcher_closed_form():
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_launcher_closed_form(path):
     """The reference launcher's workload (launcher.cpp:97-112), shrunk: exact known answer."""
     p = inputs.launcher_problem("gate_up_wgrad", G=8, M_total=8 * 1000 + 5)
     p = inputs.Problem(**{**p.__dict__, "OUT_M": 480, "OUT_N": 256,
                           "lhs": p.lhs[:, :480].contiguous(), "rhs": p.rhs[:, :256].contiguous()})
-    out = _run(p, "tcgen05").float().cpu()
+    out = _run(p, path).float().cpu()
     for g in range(p.G):
         expect = vo.closed_form_launcher_value(int(p.lens[g]))
         assert bool((out[g] == expect).all()), (g, out[g].unique()[:4], expect)
 
 
-def test_neighbour_nan_does_not_leak():
-    """Rows of the previous group that the first token block over-reads are zeroed in smem."""
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_neighbour_nan_does_not_leak(path):
+    """Rows before a group's start are never read: per-group tensor maps zero-fill them."""
     p = inputs.make_problem("tiny", seed=13, lens=[100, 50, 200], OUT_M=240, OUT_N=128)
     lhs = p.lhs.view(torch.uint8).clone()
     rhs = p.rhs.view(torch.uint8).clone()
@@ -111,19 +119,20 @@ def test_neighbour_nan_does_not_leak():
     rhs[:100] = 0x7C  # e5m2 +Inf
     q = inputs.Problem(**{**p.__dict__, "lhs": lhs.view(torch.float8_e4m3fn),
                           "rhs": rhs.view(torch.float8_e5m2)})
-    out = _run(q, "tcgen05")
+    out = _run(q, path)
     assert bool(torch.isnan(out[0].float()).any() or torch.isinf(out[0].float()).any())
     _check(q, out, groups=[1, 2], label="nan-neighbour")
 
 
-def test_padded_output_strides():
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_padded_output_strides(path):
     p = inputs.make_problem("tiny", seed=17, lens=[333, 0, 444], OUT_M=272, OUT_N=384)
     big = torch.full((3, 272 + 8, 384 + 64), 7.0, dtype=torch.bfloat16, device="cuda")
     view = big[:, :272, :384]
     assert _lib.lib().ggemm_vark_tc_supported(1 << 20, 1 << 20, view.data_ptr(), 272, 384, 272,
                                               384, view.stride(0), view.stride(1), 1) == 1
-    _run(p, "tcgen05", out=view)
-    _check(p, view, label="padded-C")
+    _run(p, path, out=view)
+    _check(p, view, label=f"padded-C/{path}")
     assert bool((big[:, 272:, :] == 7.0).all()) and bool((big[:, :, 384:] == 7.0).all())
 
 
@@ -141,16 +150,17 @@ def test_unaligned_layout_takes_simt():
     _check(p, out, label="unaligned")
 
 
-def test_bad_offsets_reported_and_zeroed():
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_bad_offsets_reported_and_zeroed(path):
     p = inputs.make_problem("tiny", seed=23, lens=[64, 64, 64, 64], OUT_M=240, OUT_N=128)
     d = p.to("cuda")
     bad = torch.tensor([0, 64, 40, 192, 256], dtype=torch.int64, device="cuda")  # 64 -> 40
     out = torch.full((4, 240, 128), 3.0, dtype=torch.bfloat16, device="cuda")
-    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, bad, out=out, path="tcgen05")
+    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, bad, out=out, path=path)
     assert _lib.read_status(clear=True) & _lib.DEV_BAD_OFFS
     assert bool((out[1] == 0).all())
     past = torch.tensor([0, 64, 128, 192, 257], dtype=torch.int64, device="cuda")  # > m_total
-    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, past, out=out, path="tcgen05")
+    vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, past, out=out, path=path)
     assert _lib.read_status(clear=True) & _lib.DEV_BAD_OFFS
     assert bool((out[3] == 0).all())
 
@@ -168,10 +178,11 @@ def test_fourteen_argument_entry_point():
     _check(p, out, label="14-arg")
 
 
-def test_deterministic():
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_deterministic(path):
     p = inputs.make_problem("tiny", seed=31, lens=[1000, 3000, 17], OUT_M=480, OUT_N=640)
-    a = _run(p, "tcgen05")
-    b = _run(p, "tcgen05")
+    a = _run(p, path)
+    b = _run(p, path)
     assert torch.equal(a, b)
 
 

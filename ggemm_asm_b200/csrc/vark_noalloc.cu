@@ -1,0 +1,204 @@
+// vark_noalloc.cu - ggemm_vark_fp8_wgrad_noalloc: the grouped wgrad without any allocation.
+//
+// Who needs this. Some callers cannot let a library call cudaMalloc: code that runs inside a
+// memory pool or arena owned by a framework (every byte must come from the arena), allocators
+// with strict accounting, processes that fixed their device footprint up front, and paths that
+// must not hit the device-wide synchronisation cudaMalloc/cudaFree can imply. The regular entry
+// points make one cudaMalloc per device on first use (status words plus the ring of tensor maps
+// the kernel builds). This entry point runs the same CTA-pair tensor-core kernel with that
+// scratch taken from a fixed, file-scope device array instead, so it never allocates.
+//
+// What it costs. The array below (NOALLOC_SCRATCH_BYTES = 516 KiB) exists on every GPU that
+// loads this library, for the life of the process, whether or not this entry point is called.
+// All calls on a device share it and it keeps the last call's contents; the status words are
+// cleared (cudaMemsetAsync on the caller's stream) at the start of every call, the tensor-map
+// ring needs no clearing (each slot is written before it is read). Calls that overlap on the
+// GPU (different streams, no ordering between them) race on the status words.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <mutex>
+
+#include "../../include/ggemm_vark.h"
+#include "vark_internal.h"
+
+namespace {
+
+constexpr int kSmIds = 256;            // SM identifiers the tensor-map ring covers
+constexpr size_t kStatusBytes = 4096;  // status words; the ring starts 4 KiB in (128-aligned)
+constexpr size_t kScratchBytes = kStatusBytes + static_cast<size_t>(kSmIds) * vark::TMAP_SLOTS *
+                                                    vark::TMAP_PAIR_BYTES;
+static_assert(kScratchBytes == GGEMM_VARK_NOALLOC_SCRATCH_BYTES, "header and file disagree");
+
+// The scratch. In host code this name is only a stand-in for the device object: the device
+// address comes from cudaGetSymbolAddress below and is what the kernel receives.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kScratchBytes];
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kTokenCoordLimit = INT32_MAX;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+struct Device {
+  bool ready = false;
+  int sm_count = 0;
+  uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+};
+
+std::mutex g_mu;
+Device g_devs[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
+
+// Once per device, with that device current: resolve the scratch array's device address and
+// the kernel attributes. Nothing here allocates.
+int setup(Device** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return GGEMM_VARK_ENO_DEVICE;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  Device& d = g_devs[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return GGEMM_VARK_ECUDA;
+    }
+    if (major != 10 || minor != 0) return GGEMM_VARK_ENO_DEVICE;
+    if (d.sm_count > kSmIds || d.sm_count < 2) return GGEMM_VARK_ETOO_LARGE;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return GGEMM_VARK_ECUDA;
+    }
+    if (vark::tc2_set_attributes() != cudaSuccess) {
+      cudaGetLastError();
+      return GGEMM_VARK_ECUDA;
+    }
+    if (g_enc == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        cudaGetLastError();
+        return GGEMM_VARK_ECUDA;
+      }
+      g_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    d.scratch = static_cast<uint8_t*>(ptr);
+    d.ready = true;
+  }
+  *out = &d;
+  return GGEMM_VARK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+CUresult encode_operand(CUtensorMap* m, const void* base, int32_t features, uint64_t tokens,
+                        int32_t pitch) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(features), tokens};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+CUresult encode_out(CUtensorMap* m, void* c, int32_t G, int32_t OUT_M, int32_t OUT_N,
+                    int32_t scg, int32_t scm) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OUT_N), static_cast<cuuint64_t>(OUT_M),
+                              static_cast<cuuint64_t>(G)};
+  const cuuint64_t strides[2] = {2ull * static_cast<cuuint64_t>(scm),
+                                 2ull * static_cast<cuuint64_t>(scg)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace
+
+extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, void* c,
+                                            const float* lhs_scale, const float* rhs_scale,
+                                            const int64_t* group_offs, int32_t G, int32_t OUT_M,
+                                            int32_t OUT_N, int32_t stride_lhs_m,
+                                            int32_t stride_rhs_m, int32_t stride_cg,
+                                            int32_t stride_cm, int32_t stride_cn,
+                                            int64_t m_total, int32_t scale_stride,
+                                            void* status, void* stream) {
+  // Same argument rules as ggemm_vark_fp8_wgrad_ex, restricted to layouts the tensor-core
+  // kernel takes (this entry point has no CUDA-core fallback).
+  if (c == nullptr || lhs_scale == nullptr || rhs_scale == nullptr || group_offs == nullptr)
+    return GGEMM_VARK_EINVAL_PTR;
+  if (lhs == nullptr || rhs == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  if (G < 0 || OUT_M <= 0 || OUT_N <= 0) return GGEMM_VARK_EINVAL_SHAPE;
+  if (stride_lhs_m < OUT_M || stride_rhs_m < OUT_N || stride_cn <= 0 || stride_cm <= 0 ||
+      stride_cg <= 0)
+    return GGEMM_VARK_EINVAL_STRIDE;
+  if ((scale_stride != 0 && scale_stride != 1) || m_total < -1) return GGEMM_VARK_EINVAL_ARG;
+  if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
+  if (!aligned16(lhs) || !aligned16(rhs) || !aligned16(c) || stride_lhs_m % 16 != 0 ||
+      stride_rhs_m % 16 != 0 || stride_cn != 1 || (2ll * stride_cm) % 16 != 0 ||
+      (2ll * stride_cg) % 16 != 0)
+    return GGEMM_VARK_ELAYOUT;
+  if (G == 0) return GGEMM_VARK_OK;
+
+  Device* d = nullptr;
+  int rc = setup(&d);
+  if (rc != GGEMM_VARK_OK) return rc;
+
+  const int32_t row_tiles = (OUT_M + 2 * vark::PAIR_HALF - 1) / (2 * vark::PAIR_HALF);
+  const int32_t col_tiles = (OUT_N + vark::PAIR_COLS - 1) / vark::PAIR_COLS;
+  const int64_t items = static_cast<int64_t>(G) * row_tiles * col_tiles;
+  if (items > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
+  // The scratch this call needs: the status words and one ring slice per SM identifier.
+  const size_t needed = kStatusBytes + vark::tc_tmap_ring_bytes(kSmIds);
+  if (needed > kScratchBytes) return GGEMM_VARK_ETOO_LARGE;
+
+  const int64_t token_limit =
+      m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
+  const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
+  CUtensorMap map_lhs, map_rhs, map_c;
+  if (encode_operand(&map_lhs, lhs, OUT_M, token_dim, stride_lhs_m) != CUDA_SUCCESS ||
+      encode_operand(&map_rhs, rhs, OUT_N, token_dim, stride_rhs_m) != CUDA_SUCCESS ||
+      encode_out(&map_c, c, G, OUT_M, OUT_N, stride_cg, stride_cm) != CUDA_SUCCESS)
+    return GGEMM_VARK_ELAYOUT;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* st = status != nullptr ? static_cast<uint32_t*>(status)
+                                   : reinterpret_cast<uint32_t*>(d->scratch);
+  if (status == nullptr && cudaMemsetAsync(d->scratch, 0, 16, s) != cudaSuccess) {
+    cudaGetLastError();
+    return GGEMM_VARK_ECUDA;
+  }
+
+  vark::TcParams tp;
+  tp.group_offs = group_offs;
+  tp.lhs_scale = lhs_scale;
+  tp.rhs_scale = rhs_scale;
+  tp.scale_stride = scale_stride;
+  tp.G = G;
+  tp.OUT_M = OUT_M;
+  tp.OUT_N = OUT_N;
+  tp.row_tiles = row_tiles;
+  tp.col_tiles = col_tiles;
+  tp.token_limit = token_limit;
+  tp.status = st;
+  tp.timeout_ns = kTimeoutNs;
+  tp.lhs = static_cast<const uint8_t*>(lhs);
+  tp.rhs = static_cast<const uint8_t*>(rhs);
+  tp.stride_lhs = stride_lhs_m;
+  tp.stride_rhs = stride_rhs_m;
+  tp.tmap_ring = d->scratch + kStatusBytes;
+  tp.num_sms = kSmIds;
+  const int64_t clusters = items < d->sm_count / 2 ? items : d->sm_count / 2;
+  const cudaError_t e =
+      vark::tc2_launch(map_lhs, map_rhs, map_c, tp, static_cast<int>(2 * clusters), s);
+  if (e != cudaSuccess) return GGEMM_VARK_ECUDA;
+  return GGEMM_VARK_OK;
+}

@@ -137,3 +137,29 @@ def test_ctypes_signatures_are_complete():
         fn = getattr(_lib.lib(), name)
         assert fn.restype == res and list(fn.argtypes) == args
     assert _lib.SIGNATURES["ggemm_vark_fp8_wgrad"][1].count(ctypes.c_int32) == 8
+
+
+def call_noalloc(**kw):
+    a = dict(lhs=P, rhs=P, c=P, ls=P, rs=P, offs=P, G=4, M=64, N=128, slm=64, srm=128,
+             scg=64 * 128, scm=128, scn=1, m_total=1024, scale_stride=0, status=None)
+    a.update(kw)
+    return _lib.lib().ggemm_vark_fp8_wgrad_noalloc(
+        a["lhs"], a["rhs"], a["c"], a["ls"], a["rs"], a["offs"], a["G"], a["M"], a["N"],
+        a["slm"], a["srm"], a["scg"], a["scm"], a["scn"], a["m_total"], a["scale_stride"],
+        a["status"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(lhs=None), _lib.EINVAL_PTR), (dict(offs=None), _lib.EINVAL_PTR),
+    (dict(G=-1), _lib.EINVAL_SHAPE), (dict(slm=32), _lib.EINVAL_STRIDE),
+    (dict(scale_stride=3), _lib.EINVAL_ARG), (dict(status=P + 4), _lib.EINVAL_ARG),
+    (dict(slm=72), _lib.ELAYOUT), (dict(c=P + 2), _lib.ELAYOUT), (dict(scn=2), _lib.ELAYOUT),
+    (dict(G=0), _lib.OK),
+])
+def test_noalloc_argument_checks(kw, code):
+    assert call_noalloc(**kw) == code
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device answer")
+def test_noalloc_without_device():
+    assert call_noalloc() == _lib.ENO_DEVICE

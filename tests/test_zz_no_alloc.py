@@ -1,0 +1,91 @@
+"""The allocation-free entry point (ggemm_vark_fp8_wgrad_noalloc).
+
+It exists for callers that must not let a library call cudaMalloc: code that runs inside a
+framework-owned memory pool or arena, allocators with strict accounting, and processes with a
+fixed device footprint. It runs the same tensor-core kernel as the regular entry points with its
+scratch in a fixed device array inside the library. This file is named so that pytest collects
+it last; it must pass alone in a fresh process and after the other tests.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from ggemm_asm_b200 import _lib, inputs
+from oracle import vark_oracle as vo
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(d, out, status=None):
+    """Call the C ABI entry point directly (no Python-side allocation on this path)."""
+    stream = torch.cuda.current_stream().cuda_stream
+    return _lib.lib().ggemm_vark_fp8_wgrad_noalloc(
+        d.lhs.data_ptr(), d.rhs.data_ptr(), out.data_ptr(), d.lhs_scale.data_ptr(),
+        d.rhs_scale.data_ptr(), d.group_offs.data_ptr(), d.G, d.OUT_M, d.OUT_N,
+        d.lhs.stride(0), d.rhs.stride(0), out.stride(0), out.stride(1), out.stride(2),
+        d.lhs.shape[0], 0 if d.lhs_scale.numel() == 1 else 1,
+        None if status is None else status.data_ptr(), stream)
+
+
+def _existing(d, out):
+    stream = torch.cuda.current_stream().cuda_stream
+    return _lib.lib().ggemm_vark_fp8_wgrad_ex(
+        d.lhs.data_ptr(), d.rhs.data_ptr(), out.data_ptr(), d.lhs_scale.data_ptr(),
+        d.rhs_scale.data_ptr(), d.group_offs.data_ptr(), d.G, d.OUT_M, d.OUT_N,
+        d.lhs.stride(0), d.rhs.stride(0), out.stride(0), out.stride(1), out.stride(2),
+        d.lhs.shape[0], 0 if d.lhs_scale.numel() == 1 else 1, _lib.PATH_AUTO, None, 0, stream)
+
+
+def _tolerance_check(p, got, ref):
+    """Within the parity tolerance used everywhere in this suite (1 bf16 ulp of the oracle's
+    magnitude plus the fp32 reassociation bound), against the regular entry point's output."""
+    ref32 = vo.wgrad_torch_f32(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
+    tol = vo.tolerance(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, ref32)
+    err = (got.float().cpu() - ref.float().cpu()).abs()
+    assert bool((err <= tol).all()), f"max diff {err.max().item()}"
+    assert vo.cosine(got.float().cpu(), ref.float().cpu()) >= 0.99999
+
+
+@pytest.mark.parametrize("scales", ["tensor", "group"])
+def test_noalloc_matches_existing_entry_point_twice(scales):
+    problems = [
+        inputs.make_problem("tiny", seed=41, lens=[700, 0, 129, 1500, 33], OUT_M=480, OUT_N=640,
+                            scales=scales),
+        inputs.make_problem("tiny", seed=42, lens=[64, 2000, 0, 0, 901], OUT_M=480, OUT_N=640,
+                            scales=scales),
+    ]
+    for p in problems:  # two calls in a row, different data: no stale state carries over
+        d = p.to("cuda")
+        ref = torch.full((d.G, d.OUT_M, d.OUT_N), 5.0, dtype=torch.bfloat16, device="cuda")
+        got = torch.full_like(ref, -5.0)
+        assert _existing(d, ref) == _lib.OK
+        assert _noalloc(d, got) == _lib.OK
+        torch.cuda.synchronize()
+        _tolerance_check(p, got, ref)
+        assert torch.equal(got, ref)  # same kernel, same accumulation order
+
+
+def test_noalloc_reports_status_in_caller_buffer():
+    p = inputs.make_problem("tiny", seed=43, lens=[64, 64, 64, 64], OUT_M=256, OUT_N=256)
+    d = p.to("cuda")
+    d.group_offs = torch.tensor([0, 64, 40, 192, 256], dtype=torch.int64, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    out = torch.full((4, 256, 256), 3.0, dtype=torch.bfloat16, device="cuda")
+    assert _noalloc(d, out, status) == _lib.OK
+    torch.cuda.synchronize()
+    assert int(status[0].item()) & _lib.DEV_BAD_OFFS
+    assert bool((out[1] == 0).all())
+
+
+def test_noalloc_rejects_what_it_cannot_run():
+    p = inputs.make_problem("tiny", seed=44, lens=[10, 20], OUT_M=64, OUT_N=128)
+    d = p.to("cuda")
+    out = torch.empty(2, 64, 128, dtype=torch.bfloat16, device="cuda")
+    wide = torch.zeros(30, 72, dtype=torch.uint8, device="cuda")
+    d.lhs = wide[:, :64].view(torch.float8_e4m3fn)  # row pitch 72: not a tensor-core layout
+    assert _noalloc(d, out) == _lib.ELAYOUT
+    assert _lib.lib().ggemm_vark_fp8_wgrad_noalloc(
+        None, None, None, None, None, None, 1, 1, 1, 1, 1, 1, 1, 1, -1, 0, None, None) == \
+        _lib.EINVAL_PTR
+    assert ctypes.c_uint32(528384).value == 516 * 1024

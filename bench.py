@@ -29,7 +29,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -93,56 +92,65 @@ def profile_traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi sampler for the timed region (clocks and throttle reasons)."""
+    """Polls NVML (SM clock, power, clock-event reasons) every `period` seconds in a thread.
+    `window(t0, t1)` summarises the samples taken between two host timestamps. NVML averages
+    each reading over its own sample period (1/6 s to 1 s), so a short timed region yields few
+    and partly averaged samples; `sustained()` reads a longer untimed stretch of the same work."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+             "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.out = None
+    def __init__(self, device: int, period: float = 0.005):
+        import threading
+
+        self.samples = []  # (t, sm_mhz, power_w, reasons_mask)
+        self.period = period
+        self.stop_ev = threading.Event()
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            self.nvml = pynvml
+            self.handle = torch.cuda._get_pynvml_handler(device)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:  # NVML unavailable: report that instead of guessing
+            self.handle = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self.nvml
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append((time.perf_counter(),
+                                     float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)),
+                                     nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0,
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle))))
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+        if self.handle is not None:
+            self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        self.stop_ev.set()
+        if self.handle is not None:
+            self.thread.join(timeout=5)
 
-    def summary(self):
-        if not self.out:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                smax = float(r[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.strip() == "Active":
-                    reasons.add(name)
-        busy = [x for x in sm if smax and x > 0.3 * smax] or sm
-        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(rows)}
+    def window(self, t0: float, t1: float) -> dict:
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        sel = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not sel:  # region shorter than the polling period: nearest sample after it
+            later = [s for s in self.samples if s[0] >= t0]
+            sel = later[:1]
+        reasons = sorted(n for n, bit in self.NAMES.items() if any(s[3] & bit for s in sel))
+        return {"sm_mhz": statistics.median(s[1] for s in sel) if sel else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(sel),
+                "power_w_max": max((s[2] for s in sel), default=None), "source": "nvml"}
 
 
 def build_problem(args, rank, world, device):
@@ -283,14 +291,27 @@ def main():
 
     # ---- kernel-only timed region -------------------------------------------------------------
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    time.sleep(0.05)
     barrier()
-    with ClockSampler(local) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
+    t_begin = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_end = time.perf_counter()
+    barrier()
+    clocks = sampler.window(t_begin, t_end)
+    # Sustained clocks: the same work continued (untimed) for about half a second.
+    t_s0 = time.perf_counter()
+    while time.perf_counter() - t_s0 < 0.5:
+        for _ in range(10):
             step()
-        ev1.record(stream)
         torch.cuda.synchronize()
-    barrier()
+    clocks_sustained = sampler.window(t_s0 + 0.2, time.perf_counter())
+    sampler.__exit__()
     ms_local = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms_local)
     flops_local = p.flops
@@ -350,7 +371,7 @@ def main():
     roofline = {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
                 "frac": achieved / fp8_peak, "traffic": profile_traffic(workload),
                 "peak_source": peak_src, "frac_of_nominal_4500": achieved / FP8_NOMINAL_TFLOPS,
-                "kernel": "vark_tc_kernel",
+                "kernel": "vark_tc2_kernel",
                 "algorithmic_unit": "2*tokens*OUT_M*OUT_N FLOP per launch (this rank)"}
 
     # ---- CPU baseline (rank 0, N=1 only) --------------------------------------------------------
@@ -381,7 +402,8 @@ def main():
                        "parallelism": f"expert-shard x{world}",
                        "l2": "inputs (1.13 GB) >> 126 MB L2; no flush"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
-            "clocks": clocks.summary(), "gpu_launches": args.steps,
+            "clocks": clocks, "clocks_sustained_untimed": clocks_sustained,
+            "gpu_launches": args.steps,
             "gpu_launches_e2e": None if e2e is None else e2e["steps"],
         }
         print(json.dumps(line), flush=True)

@@ -122,10 +122,10 @@ int check_args(const void* lhs, const void* rhs, void* c, const float* ls, const
 }
 
 CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                      uint64_t row_pitch) {
+                      uint64_t row_pitch, uint32_t box_tokens) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_pitch};
-  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(vark::TILE_TOKENS)};
+  const cuuint32_t box[2] = {128, box_tokens};
   const cuuint32_t estr[2] = {1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -219,10 +219,11 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
       pair ? encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
            : encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, vark::EPI_BOX_COLS,
                       vark::EPI_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+  const uint32_t box_tokens = pair ? vark::PAIR_TOKENS : vark::TILE_TOKENS;
   if (encode_2d_u8(&map_rhs, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
-                   static_cast<uint64_t>(srm)) != CUDA_SUCCESS ||
+                   static_cast<uint64_t>(srm), box_tokens) != CUDA_SUCCESS ||
       encode_2d_u8(&map_lhs, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                   static_cast<uint64_t>(slm)) != CUDA_SUCCESS ||
+                   static_cast<uint64_t>(slm), box_tokens) != CUDA_SUCCESS ||
       enc_c != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
 
@@ -245,6 +246,9 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.stride_rhs = srm;
   tp.tmap_ring = dev->tmap_ring;
   tp.num_sms = kTmapSmIds;
+  tp.c = static_cast<uint16_t*>(c);
+  tp.stride_cg = scg;
+  tp.stride_cm = scm;
   cudaError_t e;
   if (pair) {
     const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;

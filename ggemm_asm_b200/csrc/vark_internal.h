@@ -24,12 +24,23 @@ constexpr int LHS_BOXES = (TILE_ROWS + 127) / 128;  // 128-wide TMA boxes per LH
 
 // Geometry of the CTA-pair (cta_group::2) kernel: a work item is 256 C rows (128 per CTA) by
 // 256 C columns; 128 tokens per pipeline stage.
+#ifndef VARK_PAIR_NT
+#define VARK_PAIR_NT 1
+#endif
+// Stage shape of the pair kernel: 192 tokens (6 MMAs per commit) x 4 stages measured best on
+// B200 (81% of tensor peak in cycles at the gate_up shape vs 76% for 128 x 6 and 79% for 256 x 3):
+// fewer commit/wait hand-offs per MMA against enough stages to cover TMA latency.
 #ifndef VARK_PAIR_STAGES
-#define VARK_PAIR_STAGES 6
+#define VARK_PAIR_STAGES (VARK_PAIR_NT == 1 ? 4 : 3)
 #endif
 constexpr int PAIR_HALF = 128;
-constexpr int PAIR_COLS = 256;
+constexpr int PAIR_NT = VARK_PAIR_NT;       // 256-column MMA tiles per work item (1 or 2)
+constexpr int PAIR_COLS = 256 * PAIR_NT;    // C columns per work item
 constexpr int PAIR_STAGES = VARK_PAIR_STAGES;
+#ifndef VARK_PAIR_TK
+#define VARK_PAIR_TK 192
+#endif
+constexpr int PAIR_TOKENS = VARK_PAIR_TK;   // tokens per pipeline stage of the pair kernel
 
 // Per-SM ring of device-built tensor-map pairs (RHS, LHS) for the group being loaded.
 constexpr int TMAP_SLOTS = 8;
@@ -58,6 +69,9 @@ struct TcParams {
   int64_t stride_rhs;
   uint8_t* tmap_ring;    // num_SMs * TMAP_SLOTS * TMAP_PAIR_BYTES bytes, 128-byte aligned
   int32_t num_sms;       // SM count the ring was sized for
+  uint16_t* c;           // C (bf16 bits) and its element strides, for direct stores
+  int64_t stride_cg;
+  int64_t stride_cm;
 };
 
 // Bytes of tensor-map ring the tcgen05 kernel needs on a device with `num_sms` SMs.

@@ -101,7 +101,7 @@ CUresult encode_operand(CUtensorMap* m, const void* base, int32_t features, uint
                         int32_t pitch) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(features), tokens};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(vark::PAIR_TOKENS)};
   const cuuint32_t estr[2] = {1, 1};
   return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -196,6 +196,9 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   tp.stride_rhs = stride_rhs_m;
   tp.tmap_ring = d->scratch + kStatusBytes;
   tp.num_sms = kSmIds;
+  tp.c = static_cast<uint16_t*>(c);
+  tp.stride_cg = stride_cg;
+  tp.stride_cm = stride_cm;
   const int64_t clusters = items < d->sm_count / 2 ? items : d->sm_count / 2;
   const cudaError_t e =
       vark::tc2_launch(map_lhs, map_rhs, map_c, tp, static_cast<int>(2 * clusters), s);

@@ -223,6 +223,15 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Compiler fence on registers filled by tcgen05.ld: the asm outputs of the load look ready to
+// the compiler as soon as the load is issued, so without this a use could be scheduled before
+// tcgen05.wait::ld. Call right after tmem_ld_wait().
+template <int N>
+__device__ __forceinline__ void tmem_regs_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Clusters of two CTAs (cta_group::2). No TMA multicast is used anywhere in this library.
 // ---------------------------------------------------------------------------------------------

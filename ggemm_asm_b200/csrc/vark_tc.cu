@@ -360,6 +360,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t r[16];
           tmem_ld_32x32b_x16(t_acc + c * EPI_BOX_ROWS, r);
           tmem_ld_wait();
+          tmem_regs_fence(r);
           const uint32_t buf = nstore & 1u;
           if (lane == 0) bulk_wait_group_read<1>();  // the store that used `buf` has read it
           __syncwarp();

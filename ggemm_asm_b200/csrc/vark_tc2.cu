@@ -50,30 +50,37 @@
 namespace vark {
 namespace {
 
-constexpr int NUM_THREADS = 192;
+#ifndef VARK_PAIR_EPI_WARPS
+#define VARK_PAIR_EPI_WARPS 4
+#endif
 constexpr int EPI_WARP0 = 2;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = VARK_PAIR_EPI_WARPS;  // 4 or 8: one or two warps per TMEM lane quarter
+constexpr int EPI_SPLIT = EPI_WARPS / 4;        // warps sharing one lane quarter's columns
+constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
 constexpr int PAIR_ROWS = 2 * PAIR_HALF;   // C rows per work item (MMA M)
-constexpr int TILE_N2 = PAIR_COLS;         // C columns per work item (MMA N)
-constexpr int TK = 128;                    // tokens per stage
+constexpr int NT = PAIR_NT;                // N=256 MMAs per 32 tokens (share the A operand)
+constexpr int TILE_N2 = PAIR_COLS;         // C columns per work item (NT x 256)
+constexpr int NACC = 2 / NT;               // TMEM accumulators (double-buffered when NT == 1)
+constexpr int TK = PAIR_TOKENS;            // tokens per stage (128 or 256: 4 or 8 MMAs)
 constexpr int ST = PAIR_STAGES;
 
 constexpr uint32_t BOX_BYTES = 128 * TK;                 // 16 KiB per operand box
-constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;          // LHS box + RHS box
-constexpr uint32_t ACC_COLS = 256;
+constexpr uint32_t STAGE_BYTES = (1 + NT) * BOX_BYTES;   // LHS box + NT RHS boxes
+constexpr uint32_t ACC_COLS = 256 * NT;                 // TMEM columns per accumulator
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int EPI_COLS = 32;                             // C columns per epilogue box
 constexpr int EPI_ROWS = 32;                             // C rows per epilogue box (one warp)
 constexpr uint32_t EPI_BUF_BYTES = EPI_COLS * EPI_ROWS * 2;  // 2 KiB
 
-static_assert(PAIR_HALF == 128 && PAIR_COLS == 256, "pair tile is 256 x 256");
+static_assert(PAIR_HALF == 128 && (NT == 1 || NT == 2), "pair tile is 256 x (256 or 512)");
+static_assert(TK % 32 == 0 && TK >= 64 && TK <= 256, "token block: a multiple of the MMA K (32), TMA box rows <= 256");
 
 // Shared-memory map (offsets from a 1024-byte aligned base; identical in both CTAs).
 constexpr uint32_t OFF_LHS = 0;
 constexpr uint32_t OFF_RHS = OFF_LHS + ST * BOX_BYTES;
-constexpr uint32_t OFF_EPI = OFF_RHS + ST * BOX_BYTES;
-constexpr uint32_t OFF_ZERO = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t OFF_TMAP = OFF_ZERO + EPI_BUF_BYTES;
+constexpr uint32_t OFF_EPI = OFF_RHS + ST * NT * BOX_BYTES;
+constexpr uint32_t OFF_TMAP = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
 constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
 constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
@@ -83,7 +90,7 @@ static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0, "alignment");
 
 constexpr uint32_t IDESC = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
-                                        /*A MN-major*/ 1, /*B MN-major*/ 1, PAIR_ROWS, TILE_N2);
+                                        /*A MN-major*/ 1, /*B MN-major*/ 1, PAIR_ROWS, 256);
 
 struct Ctl {
   volatile int* abort;
@@ -167,18 +174,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(sbase + OFF_MISC + 4);
 
   // ---- set-up -------------------------------------------------------------------------------
-  {
-    uint32_t* z = reinterpret_cast<uint32_t*>(sbase + OFF_ZERO);
-    for (int i = threadIdx.x; i < static_cast<int>(EPI_BUF_BYTES / 4); i += NUM_THREADS) z[i] = 0u;
-    fence_proxy_async_smem();
-  }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int s = 0; s < ST; ++s) {
       mbar_init(bar_full + 8 * s, 2);   // one expect-tx arrival from each CTA's producer
       mbar_init(bar_empty + 8 * s, 1);  // the leader's commit
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);                // the leader's commit
       mbar_init(bar_tempty + 8 * a, 2 * EPI_WARPS);   // every epilogue warp of the pair
     }
@@ -258,7 +260,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
           const int32_t y = y0 + TK * kb;
           tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, gmap_lhs, fb, xl, y, policy);
-          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, gmap_rhs, fb, xr, y, policy);
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+            tma_load_2d_pair(base + OFF_RHS + (stage * NT + j) * BOX_BYTES, gmap_rhs, fb,
+                             xr + 256 * j, y, policy);
         }
         __syncwarp();
         if (++stage == ST) {
@@ -302,13 +307,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after_sync();
           const uint32_t a_stage = base + OFF_LHS + stage * BOX_BYTES;
-          const uint32_t b_stage = base + OFF_RHS + stage * BOX_BYTES;
+          const uint32_t b_stage = base + OFF_RHS + stage * NT * BOX_BYTES;
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < TK / 32; ++ks) {
               const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
-              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
-              mma_f8f6f4_pair(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+              for (int j = 0; j < NT; ++j) {
+                const uint64_t bdesc =
+                    smem_desc_sw128(b_stage + j * BOX_BYTES + ks * 4096u, BOX_BYTES, 1024u);
+                mma_f8f6f4_pair(d_tmem + 256u * j, adesc, bdesc, IDESC,
+                                (kb > 0 || ks > 0) ? 1u : 0u);
+              }
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
           }
@@ -321,8 +331,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!ok) break;
         if (lane == 0) mma_commit_pair(bar_tfull + 8 * acc, 0x3);  // accumulator ready
         __syncwarp();
-        acc ^= 1u;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       if (lane == 0) {
         mma_commit_pair(bar_drain, 0x1);
@@ -334,28 +346,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
     }
   } else {
-    // ======================= epilogue (warps 2..5, both CTAs) ===============================
+    // ======================= epilogue (EPI_WARPS warps, both CTAs) ===========================
     const int ew = warp - EPI_WARP0;
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int quarter = warp & 3;        // TMEM lanes this warp may access
+    const int half = ew >> 2;            // which of the quarter's warps (0 when EPI_SPLIT == 1)
     const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t zero_buf = base + OFF_ZERO;
     const uint32_t epi_sh = base + OFF_EPI + ew * 2 * EPI_BUF_BYTES;
     const uint32_t leader_tempty = mapa_shared(bar_tempty, 0);
     uint32_t acc = 0, acc_phase = 0;
     uint32_t nstore = 0;
+    // Next free staging buffer: wait until the TMA store that last read it has finished.
+    auto next_buf = [&]() -> uint32_t {
+      const uint32_t buf = epi_sh + (nstore & 1u) * EPI_BUF_BYTES;
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      return buf;
+    };
     for (int item = cluster; item < num_items; item += nclusters) {
-      const Item t = decode_item(p, item, leader && quarter == 0 && lane == 0);
+      const Item t = decode_item(p, item, leader && ew == 0 && lane == 0);
       const int yrow = t.m0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C row
       const bool rows_live = yrow < p.OUT_M;
       const int cols_here = min(TILE_N2, p.OUT_N - t.n0);
       const int nchunks = (cols_here + EPI_COLS - 1) / EPI_COLS;
       if (t.tokens == 0) {
-        if (rows_live && lane == 0) {
-          for (int c = 0; c < nchunks; ++c)
-            tma_store_3d(&map_c, zero_buf, t.n0 + c * EPI_COLS, yrow, t.g);
-          bulk_commit_group();
+        if (rows_live) {
+          const uint32_t buf = next_buf();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(
+                             buf + static_cast<uint32_t>(lane) * 64u + k * 16u),
+                         "r"(0u)
+                         : "memory");
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int c = half; c < nchunks; c += EPI_SPLIT)
+              tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, yrow, t.g);
+            bulk_commit_group();
+          }
+          ++nstore;
         }
-        __syncwarp();
         continue;
       }
       const float scale = __ldg(p.lhs_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
@@ -364,15 +394,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after_sync();
       if (rows_live) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_acc + c * EPI_COLS, r);
-          tmem_ld_wait();
-          const uint32_t buf = epi_sh + (nstore & 1u) * EPI_BUF_BYTES;
-          if (lane == 0) bulk_wait_group_read<1>();  // the store that used `buf` has read it
-          __syncwarp();
-          // Row `lane` of the 32x32 box: 64 bytes = four 16-byte chunks, stored with the
-          // 64-byte swizzle (chunk ^= (row >> 1) & 3) that the C tensor map expects.
+        // Row `lane` of a 32x32 C box: 64 bytes = four 16-byte chunks, stored with the 64-byte
+        // swizzle (chunk ^= (row >> 1) & 3) that the C tensor map expects, then TMA-stored.
+        auto emit = [&](uint32_t (&r)[32], int c) {
+          const uint32_t buf = next_buf();
           const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
           const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
 #pragma unroll
@@ -397,13 +422,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             bulk_commit_group();
           }
           ++nstore;
+        };
+        // Two register sets: the load of the next chunk overlaps the conversion of this one.
+        uint32_t ra[32], rb[32];
+        int c = half;
+        if (c < nchunks) tmem_ld_32x32b_x32(t_acc + c * EPI_COLS, ra);
+        tmem_ld_wait();
+        tmem_regs_fence(ra);
+        while (c < nchunks) {
+          int cn = c + EPI_SPLIT;
+          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_COLS, rb);
+          emit(ra, c);
+          tmem_ld_wait();
+          tmem_regs_fence(rb);
+          c = cn;
+          if (c >= nchunks) break;
+          cn = c + EPI_SPLIT;
+          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_COLS, ra);
+          emit(rb, c);
+          tmem_ld_wait();
+          tmem_regs_fence(ra);
+          c = cn;
         }
       }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty + 8 * acc);
-      acc ^= 1u;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();

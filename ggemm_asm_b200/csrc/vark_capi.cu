@@ -202,7 +202,7 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
 
   // Tensor-core paths.
   const bool pair = path != GGEMM_VARK_PATH_TCGEN05_1SM && dev->sm_count >= 2;
-  const int32_t rt = pair ? 2 * vark::PAIR_HALF : vark::TILE_ROWS;
+  const int32_t rt = pair ? vark::PAIR_ROWS_MAX : vark::TILE_ROWS;
   const int32_t ct = pair ? vark::PAIR_COLS : vark::TILE_COLS;
   const int32_t row_tiles = (OUT_M + rt - 1) / rt;
   const int32_t col_tiles = (OUT_N + ct - 1) / ct;

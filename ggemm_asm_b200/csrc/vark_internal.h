@@ -22,24 +22,21 @@ constexpr int TILE_TOKENS = VARK_TILE_TOKENS;  // 64 or 128 (a multiple of the M
 constexpr int STAGES = VARK_STAGES;
 constexpr int LHS_BOXES = (TILE_ROWS + 127) / 128;  // 128-wide TMA boxes per LHS stage
 
-// Geometry of the CTA-pair (cta_group::2) kernel: a work item is 256 C rows (128 per CTA) by
-// 256 C columns; 128 tokens per pipeline stage.
-#ifndef VARK_PAIR_NT
-#define VARK_PAIR_NT 1
-#endif
-// Stage shape of the pair kernel: 192 tokens (6 MMAs per commit) x 4 stages measured best on
-// B200 (81% of tensor peak in cycles at the gate_up shape vs 76% for 128 x 6 and 79% for 256 x 3):
-// fewer commit/wait hand-offs per MMA against enough stages to cover TMA latency.
-#ifndef VARK_PAIR_STAGES
-#define VARK_PAIR_STAGES (VARK_PAIR_NT == 1 ? 4 : 3)
-#endif
-constexpr int PAIR_HALF = 128;
-constexpr int PAIR_NT = VARK_PAIR_NT;       // 256-column MMA tiles per work item (1 or 2)
-constexpr int PAIR_COLS = 256 * PAIR_NT;    // C columns per work item
-constexpr int PAIR_STAGES = VARK_PAIR_STAGES;
+// Geometry of the CTA-pair (cta_group::2) kernel: a work item is 256 C columns (128 per CTA,
+// the MMA M) by up to 256 C rows (the MMA N); PAIR_TOKENS tokens per pipeline stage.
+// Stage shape: 192 tokens (6 MMAs per commit) x 4 stages measured best on B200 (81-84% of the
+// tensor peak in cycles at the gate_up shape vs 76% for 128 x 6 and 79% for 256 x 3): fewer
+// commit/wait hand-offs per MMA against enough stages to cover TMA latency.
 #ifndef VARK_PAIR_TK
 #define VARK_PAIR_TK 192
 #endif
+#ifndef VARK_PAIR_STAGES
+#define VARK_PAIR_STAGES 4
+#endif
+constexpr int PAIR_HALF = 128;              // C columns per CTA of a pair
+constexpr int PAIR_COLS = 2 * PAIR_HALF;    // C columns per work item
+constexpr int PAIR_ROWS_MAX = 256;          // C rows per work item (the last one may be fewer)
+constexpr int PAIR_STAGES = VARK_PAIR_STAGES;
 constexpr int PAIR_TOKENS = VARK_PAIR_TK;   // tokens per pipeline stage of the pair kernel
 
 // Per-SM ring of device-built tensor-map pairs (RHS, LHS) for the group being loaded.
@@ -106,8 +103,9 @@ cudaError_t simt_launch(const SimtParams& p, cudaStream_t stream);
 // Raise the tcgen05 kernel's dynamic shared-memory limit (once per device).
 cudaError_t tc_set_attributes();
 
-// CTA-pair kernel (vark_tc2.cu): same parameters; row_tiles/col_tiles count 256-wide tiles and
-// `grid` must be even (one cluster of two CTAs per pair of SMs).
+// CTA-pair kernel (vark_tc2.cu): same parameters; row_tiles = ceil(OUT_M / PAIR_ROWS_MAX),
+// col_tiles = ceil(OUT_N / PAIR_COLS), and `grid` must be even (one cluster of two CTAs per pair
+// of SMs).
 size_t tc2_smem_bytes();
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        const CUtensorMap& map_c, const TcParams& p, int grid,

@@ -152,7 +152,7 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   int rc = setup(&d);
   if (rc != GGEMM_VARK_OK) return rc;
 
-  const int32_t row_tiles = (OUT_M + 2 * vark::PAIR_HALF - 1) / (2 * vark::PAIR_HALF);
+  const int32_t row_tiles = (OUT_M + vark::PAIR_ROWS_MAX - 1) / vark::PAIR_ROWS_MAX;
   const int32_t col_tiles = (OUT_N + vark::PAIR_COLS - 1) / vark::PAIR_COLS;
   const int64_t items = static_cast<int64_t>(G) * row_tiles * col_tiles;
   if (items > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;

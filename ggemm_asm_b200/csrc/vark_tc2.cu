@@ -4,37 +4,39 @@
 // Computes, for every group g, C[g] = sL*sR * LHS[off_g:off_{g+1}]^T . RHS[off_g:off_{g+1}]
 // (ggemm-asm README.md:5,45-48; bench.py:182-193 "dW = lhs^T @ rhs" per expert).
 //
-// Tile and operands. One work item is (group g, 256 rows of C, 256 columns of C) and is computed
-// by a cluster of two CTAs with one tcgen05.mma.cta_group::2 (M=256, N=256, K=32) per 32 tokens:
-//   * MMA-M runs along OUT_M (C rows): operand A = LHS (e4m3). CTA r of the pair holds rows
-//     [m0 + 128r, m0 + 128r + 128) of the tile and its TMEM accumulates those 128 C rows.
-//   * MMA-N runs along OUT_N (C columns): operand B = RHS (e5m2). CTA r holds columns
-//     [n0 + 128r, n0 + 128r + 128); the MMA reads both halves across the pair.
+// Tile and operands. One work item is (group g, 256 columns of C, up to 256 rows of C) and is
+// computed by a cluster of two CTAs with tcgen05.mma.cta_group::2 (M=256, N<=256, K=32):
+//   * MMA-M runs along OUT_N (C columns): operand A = RHS (e5m2). CTA r of the pair holds C
+//     columns [n0 + 128r, n0 + 128r + 128) and its TMEM accumulates those 128 columns (one per
+//     TMEM lane).
+//   * MMA-N runs along OUT_M (C rows): operand B = LHS (e4m3). The N rows of the item are split
+//     N/2 per CTA; the MMA reads both halves across the pair. N is 256 except for the last row
+//     tile, where it is the remaining rows rounded up to 32 (64 for OUT_M = 2880 = 11x256 + 64),
+//     so ragged OUT_M costs no tensor work. Along OUT_N the waste is at most one 128-column half
+//     (2.2% at 5760 = 45 x 128).
 // Both operands stay in their token-major layout, which for the MMA is MN-major: a TMA box of
-// 128 contiguous features x 128 tokens lands with the 128-byte swizzle of the canonical
-// MN-major layout. Per CTA and 128 tokens that is 32 KiB (16 KiB of each operand) for
-// 128x256x128 MACs, two thirds of the bytes per MAC of a single-CTA 128x240 tile; the kernel is
-// bound by how fast one SM can ingest TMA data from L2, so bytes per MAC set the speed.
-// Shapes that are not multiples of 256 (2880 = 11.25 x 256, 5760 = 22.5 x 256) get boxes that
-// run past the tensor edge: TMA fills them with zeros without reading memory and the epilogue's
-// TMA store clips them, so only tensor-core time is spent on them.
+// 128 contiguous features x TK tokens lands with the 128-byte swizzle of the canonical MN-major
+// layout. Per CTA and TK tokens that is 2 x 128 x TK bytes for 128 x 256 x TK MACs. Boxes that
+// run past a tensor edge are zero-filled by TMA without memory traffic; the epilogue's TMA
+// stores clip them.
 //
-// Warp roles (192 threads per CTA, one CTA per SM, 74 pairs on 148 SMs, persistent over a
-// static round-robin schedule of work items by cluster):
-//   warp 0      TMA producer (both CTAs): 6-stage ring of {LHS 128x128, RHS 128x128} blocks,
+// Warp roles (64 + 32 x EPI_WARPS threads per CTA, one CTA per SM, 74 pairs on 148 SMs,
+// persistent over a static round-robin schedule of work items by cluster):
+//   warp 0      TMA producer (both CTAs): ring of ST stages {RHS 128 x TK, LHS 128 x TK},
 //               completion counted on the pair leader's full barrier
 //   warp 1      TMEM owner (both CTAs, cta_group::2 allocation of all 512 columns = two
-//               128x256 fp32 accumulators); in the leader also the MMA issuer
-//   warps 2..5  epilogue (both CTAs): tcgen05.ld 32 columns -> * (sL*sR) -> bf16 (RNE) ->
-//               64B-swizzled smem box (32x32) -> TMA store; warp w owns TMEM lanes
-//               32*(w%4)..+31 = 32 rows of this CTA's half of the tile
+//               128-lane x 256-column fp32 accumulators); in the leader also the MMA issuer
+//   warps 2..   epilogue (both CTAs): tcgen05.ld 32 TMEM columns (= 32 C rows of this lane's C
+//               column) -> * (sL*sR) -> bf16 (RNE) -> transposed into a 64B-swizzled 32x32 smem
+//               box (lane pairs exchange values so each lane writes 4-byte words) -> TMA store;
+//               warp w owns TMEM lanes 32*(w%4)..+31 = 32 C columns of this CTA's half
 // The leader's commits arrive on both CTAs' barriers (tcgen05.commit multicast); the epilogue
 // warps of both CTAs release an accumulator on the leader's barrier.
 //
-// Variable K. As in the single-CTA kernel (vark_tc.cu): token blocks of 128 aligned to the END
-// of the group, loads through per-group tensor maps built on the device (base at row off_g,
-// token extent K_g), so the partial first block starts at a negative coordinate and TMA fills
-// the rows before the group with zeros; every stage is a uniform 4 MMAs. Empty groups skip the
+// Variable K. As in the single-CTA kernel (vark_tc.cu): token blocks aligned to the END of the
+// group, loads through per-group tensor maps built on the device (base at row off_g, token
+// extent K_g), so the partial first block starts at a negative coordinate and TMA fills the
+// rows before the group with zeros; every stage is a uniform TK/32 MMAs. Empty groups skip the
 // pipeline and the epilogue stores zeros.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
@@ -58,28 +60,27 @@ constexpr int EPI_WARPS = VARK_PAIR_EPI_WARPS;  // 4 or 8: one or two warps per 
 constexpr int EPI_SPLIT = EPI_WARPS / 4;        // warps sharing one lane quarter's columns
 constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
 static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
-constexpr int PAIR_ROWS = 2 * PAIR_HALF;   // C rows per work item (MMA M)
-constexpr int NT = PAIR_NT;                // N=256 MMAs per 32 tokens (share the A operand)
-constexpr int TILE_N2 = PAIR_COLS;         // C columns per work item (NT x 256)
-constexpr int NACC = 2 / NT;               // TMEM accumulators (double-buffered when NT == 1)
-constexpr int TK = PAIR_TOKENS;            // tokens per stage (128 or 256: 4 or 8 MMAs)
+constexpr int ITEM_COLS = 2 * PAIR_HALF;   // C columns per work item (MMA M)
+constexpr int ITEM_ROWS = PAIR_ROWS_MAX;   // C rows per work item at most (MMA N)
+constexpr int TK = PAIR_TOKENS;            // tokens per stage (TK/32 MMAs)
 constexpr int ST = PAIR_STAGES;
 
-constexpr uint32_t BOX_BYTES = 128 * TK;                 // 16 KiB per operand box
-constexpr uint32_t STAGE_BYTES = (1 + NT) * BOX_BYTES;   // LHS box + NT RHS boxes
-constexpr uint32_t ACC_COLS = 256 * NT;                 // TMEM columns per accumulator
+constexpr uint32_t BOX_BYTES = 128 * TK;                 // one operand box per CTA
+constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;          // RHS box + LHS box
+constexpr uint32_t ACC_COLS = 256;                       // TMEM columns per accumulator
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int EPI_COLS = 32;                             // C columns per epilogue box
-constexpr int EPI_ROWS = 32;                             // C rows per epilogue box (one warp)
+constexpr int NACC = 2;
+constexpr int EPI_COLS = 32;                             // C columns per epilogue box (one warp)
+constexpr int EPI_ROWS = 32;                             // C rows per epilogue box
 constexpr uint32_t EPI_BUF_BYTES = EPI_COLS * EPI_ROWS * 2;  // 2 KiB
 
-static_assert(PAIR_HALF == 128 && (NT == 1 || NT == 2), "pair tile is 256 x (256 or 512)");
+static_assert(PAIR_HALF == 128 && ITEM_ROWS == 256, "pair tile is 256 x 256");
 static_assert(TK % 32 == 0 && TK >= 64 && TK <= 256, "token block: a multiple of the MMA K (32), TMA box rows <= 256");
 
 // Shared-memory map (offsets from a 1024-byte aligned base; identical in both CTAs).
-constexpr uint32_t OFF_LHS = 0;
-constexpr uint32_t OFF_RHS = OFF_LHS + ST * BOX_BYTES;
-constexpr uint32_t OFF_EPI = OFF_RHS + ST * NT * BOX_BYTES;
+constexpr uint32_t OFF_RHS = 0;                          // operand A stages
+constexpr uint32_t OFF_LHS = OFF_RHS + ST * BOX_BYTES;   // operand B stages
+constexpr uint32_t OFF_EPI = OFF_LHS + ST * BOX_BYTES;
 constexpr uint32_t OFF_TMAP = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
 constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
 constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1;
@@ -89,8 +90,9 @@ constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0, "alignment");
 
-constexpr uint32_t IDESC = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
-                                        /*A MN-major*/ 1, /*B MN-major*/ 1, PAIR_ROWS, 256);
+// Instruction descriptor without N: the item's N is or-ed in at run time.
+constexpr uint32_t IDESC_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
+                                             /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
 
 struct Ctl {
   volatile int* abort;
@@ -127,6 +129,7 @@ __device__ __forceinline__ bool warp_wait(const Ctl& ctl, uint32_t bar, uint32_t
 
 struct Item {
   int g, m0, n0;   // group, first C row, first C column of the pair tile
+  int nrows;       // MMA N: C rows of the item, a multiple of 32 (<= 256)
   int tokens;      // K_g (0 for empty or invalid groups)
   int64_t end;     // off_{g+1}
 };
@@ -136,8 +139,9 @@ __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool re
   Item t;
   t.g = item / per_group;
   const int r = item - t.g * per_group;
-  t.n0 = (r % p.col_tiles) * TILE_N2;
-  t.m0 = (r / p.col_tiles) * PAIR_ROWS;
+  t.n0 = (r % p.col_tiles) * ITEM_COLS;
+  t.m0 = (r / p.col_tiles) * ITEM_ROWS;
+  t.nrows = min(ITEM_ROWS, (p.OUT_M - t.m0 + 31) & ~31);
   const int64_t lo = __ldg(p.group_offs + t.g);
   const int64_t hi = __ldg(p.group_offs + t.g + 1);
   if (lo < 0 || hi < lo || hi > p.token_limit) {
@@ -223,22 +227,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         uint8_t* const pair =
             p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
         if (lane < 16) {
-          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_lhs : &map_rhs);
+          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_rhs : &map_lhs);
           reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
         }
         __syncwarp();
         if (lane == 0) {
           const int64_t lo = t.end - t.tokens;
-          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
+          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
           tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
-          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
+          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
           tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
         }
         __syncwarp();
         tmap_publish(pair, smem_maps);
         tmap_publish(pair + 128, smem_maps + 128);
-        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair);
-        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
+        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair);
+        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
         if (lane == 0) {
           tmap_acquire(gmap_lhs);
           tmap_acquire(gmap_rhs);
@@ -248,8 +252,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       const int nkb = (t.tokens + TK - 1) / TK;
       const int32_t y0 = t.tokens - TK * nkb;  // <= 0: rows before the group read as zeros
-      const int32_t xl = t.m0 + PAIR_HALF * static_cast<int32_t>(rank);
+      // A: this CTA's 128 C columns; B: this CTA's half of the item's rows (N/2 is a multiple
+      // of 16, so the TMA x coordinate stays 16-byte aligned).
       const int32_t xr = t.n0 + PAIR_HALF * static_cast<int32_t>(rank);
+      const int32_t xl = t.m0 + (t.nrows >> 1) * static_cast<int32_t>(rank);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
           ok = false;
@@ -259,11 +265,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
           mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
           const int32_t y = y0 + TK * kb;
+          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, gmap_rhs, fb, xr, y, policy);
           tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, gmap_lhs, fb, xl, y, policy);
-#pragma unroll
-          for (int j = 0; j < NT; ++j)
-            tma_load_2d_pair(base + OFF_RHS + (stage * NT + j) * BOX_BYTES, gmap_rhs, fb,
-                             xr + 256 * j, y, policy);
         }
         __syncwarp();
         if (++stage == ST) {
@@ -300,25 +303,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        const uint32_t idesc = IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint32_t a_stage = base + OFF_LHS + stage * BOX_BYTES;
-          const uint32_t b_stage = base + OFF_RHS + stage * NT * BOX_BYTES;
+          const uint32_t a_stage = base + OFF_RHS + stage * BOX_BYTES;
+          const uint32_t b_stage = base + OFF_LHS + stage * BOX_BYTES;
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < TK / 32; ++ks) {
               const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
-#pragma unroll
-              for (int j = 0; j < NT; ++j) {
-                const uint64_t bdesc =
-                    smem_desc_sw128(b_stage + j * BOX_BYTES + ks * 4096u, BOX_BYTES, 1024u);
-                mma_f8f6f4_pair(d_tmem + 256u * j, adesc, bdesc, IDESC,
-                                (kb > 0 || ks > 0) ? 1u : 0u);
-              }
+              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
+              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
           }
@@ -364,12 +363,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     };
     for (int item = cluster; item < num_items; item += nclusters) {
       const Item t = decode_item(p, item, leader && ew == 0 && lane == 0);
-      const int yrow = t.m0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C row
-      const bool rows_live = yrow < p.OUT_M;
-      const int cols_here = min(TILE_N2, p.OUT_N - t.n0);
-      const int nchunks = (cols_here + EPI_COLS - 1) / EPI_COLS;
+      const int xcol = t.n0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C col
+      const bool cols_live = xcol < p.OUT_N;
+      const int rows_here = min(t.nrows, p.OUT_M - t.m0);
+      const int nchunks = (rows_here + EPI_ROWS - 1) / EPI_ROWS;
       if (t.tokens == 0) {
-        if (rows_live) {
+        if (cols_live) {
           const uint32_t buf = next_buf();
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -381,7 +380,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             for (int c = half; c < nchunks; c += EPI_SPLIT)
-              tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, yrow, t.g);
+              tma_store_3d(&map_c, buf, xcol, t.m0 + c * EPI_ROWS, t.g);
             bulk_commit_group();
           }
           ++nstore;
@@ -392,33 +391,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                           __ldg(p.rhs_scale + static_cast<int64_t>(t.g) * p.scale_stride);
       if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
-      if (rows_live) {
+      if (cols_live) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
-        // Row `lane` of a 32x32 C box: 64 bytes = four 16-byte chunks, stored with the 64-byte
-        // swizzle (chunk ^= (row >> 1) & 3) that the C tensor map expects, then TMA-stored.
+        // This lane holds C column xcol + lane for the 32 C rows of TMEM columns [32c, 32c+32).
+        // The 32x32 box is stored row-major (64-byte rows) with the 64-byte swizzle the C tensor
+        // map expects (16-byte chunk ^= (row >> 1) & 3). Lanes 2i and 2i+1 (columns 2i, 2i+1)
+        // swap one value per row pair so that each writes a 4-byte word of one row: the even
+        // lane row j, the odd lane row j+1 - 32 lanes cover two 64-byte rows, no bank conflict.
+        const uint32_t pr = static_cast<uint32_t>(lane) >> 1;  // column pair index i
+        const uint32_t odd = static_cast<uint32_t>(lane) & 1u;
         auto emit = [&](uint32_t (&r)[32], int c) {
           const uint32_t buf = next_buf();
-          const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
-          const uint32_t sw = (static_cast<uint32_t>(lane) >> 1) & 3u;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            uint32_t w[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const __nv_bfloat162 v = __floats2bfloat162_rn(
-                  __uint_as_float(r[ch * 8 + 2 * k]) * scale,
-                  __uint_as_float(r[ch * 8 + 2 * k + 1]) * scale);
-              w[k] = *reinterpret_cast<const uint32_t*>(&v);
-            }
-            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
-                             row_addr + ((static_cast<uint32_t>(ch) ^ sw) << 4)),
-                         "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+          for (int j = 0; j < 32; j += 2) {
+            const float v0 = __uint_as_float(r[j]) * scale;
+            const float v1 = __uint_as_float(r[j + 1]) * scale;
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+            const __nv_bfloat162 w =
+                odd ? __floats2bfloat162_rn(other, v1) : __floats2bfloat162_rn(v0, other);
+            const uint32_t row = static_cast<uint32_t>(j) + odd;
+            const uint32_t addr = buf + row * 64u + ((((pr >> 2) ^ (row >> 1)) & 3u) << 4) +
+                                  (pr & 3u) * 4u;
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr),
+                         "r"(*reinterpret_cast<const uint32_t*>(&w))
                          : "memory");
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, yrow, t.g);
+            tma_store_3d(&map_c, buf, xcol, t.m0 + c * EPI_ROWS, t.g);
             bulk_commit_group();
           }
           ++nstore;
@@ -426,19 +427,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // Two register sets: the load of the next chunk overlaps the conversion of this one.
         uint32_t ra[32], rb[32];
         int c = half;
-        if (c < nchunks) tmem_ld_32x32b_x32(t_acc + c * EPI_COLS, ra);
+        if (c < nchunks) tmem_ld_32x32b_x32(t_acc + c * EPI_ROWS, ra);
         tmem_ld_wait();
         tmem_regs_fence(ra);
         while (c < nchunks) {
           int cn = c + EPI_SPLIT;
-          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_COLS, rb);
+          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_ROWS, rb);
           emit(ra, c);
           tmem_ld_wait();
           tmem_regs_fence(rb);
           c = cn;
           if (c >= nchunks) break;
           cn = c + EPI_SPLIT;
-          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_COLS, ra);
+          if (cn < nchunks) tmem_ld_32x32b_x32(t_acc + cn * EPI_ROWS, ra);
           emit(rb, c);
           tmem_ld_wait();
           tmem_regs_fence(ra);

@@ -193,6 +193,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ======================= TMA producer (lane 0 issues; the warp stays converged) ==========
     const uint64_t policy = l2_policy_evict_last();
     const uint32_t smid = sm_id();
+    // Failure-detection test hook (GGEMM_VARK_TEST_STALL_MAGIC): withhold the first stage.
+    bool withhold =
+        p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
+                                   GGEMM_VARK_TEST_STALL_MAGIC;
     const uint32_t smem_maps = base + OFF_TMAP;
     uint32_t stage = 0, phase = 0;
     uint32_t used_mask = 0, parity_mask = 0;  // per stage: issued at least once / last parity
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        if (lane == 0) {
+        if (lane == 0 && !withhold) {
           const uint32_t fb = bar_full + 8 * stage;
           mbar_arrive_expect_tx(fb, STAGE_TX_BYTES);
           const int32_t y = y0 + TILE_TOKENS * kb;
@@ -253,6 +257,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                              gmap_lhs, fb, t.row0 + 128 * b, y, policy);
         }
         __syncwarp();
+        withhold = false;
         used_mask |= 1u << stage;
         parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) {

@@ -211,6 +211,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // ======================= TMA producer (both CTAs) =======================================
     const uint64_t policy = l2_policy_evict_last();
     const uint32_t smid = sm_id();
+    // Failure-detection test hook (GGEMM_VARK_TEST_STALL_MAGIC): withhold the first stage.
+    bool withhold =
+        p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
+                                   GGEMM_VARK_TEST_STALL_MAGIC;
     const uint32_t smem_maps = base + OFF_TMAP;
     uint32_t stage = 0, phase = 0;
     int cur_group = -1;
@@ -261,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        if (lane == 0) {
+        if (lane == 0 && !withhold) {
           const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
           mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
           const int32_t y = y0 + TK * kb;
@@ -269,6 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, gmap_lhs, fb, xl, y, policy);
         }
         __syncwarp();
+        withhold = false;
         if (++stage == ST) {
           stage = 0;
           phase ^= 1u;

@@ -58,6 +58,14 @@ extern "C" {
 #define GGEMM_VARK_DEV_BAD_OFFS   0x1u   /* group_offs not monotone, negative, or past m_total */
 #define GGEMM_VARK_DEV_TIMEOUT    0x2u   /* a pipeline wait exceeded its limit; the CTA stopped */
 
+/* ---- test hook for failure detection ------------------------------------------------------
+ * If word 3 of a caller-provided status block (ggemm_vark_fp8_wgrad_ex's `status`) holds this
+ * value, the tensor-core kernels withhold their first pipeline stage, so the MMA warp's bounded
+ * wait expires after `timeout_ns`: every CTA stops, and the call reports GGEMM_VARK_DEV_TIMEOUT
+ * in word 0 (C is left incomplete). Nothing faults or hangs; the context stays usable. Only the
+ * failure-detection tests set it. */
+#define GGEMM_VARK_TEST_STALL_MAGIC 0x5374616cu
+
 /* ---- path selection flags for ggemm_vark_fp8_wgrad_ex ------------------------------------ */
 #define GGEMM_VARK_PATH_AUTO      0      /* tensor-core path when the layout allows, else SIMT */
 #define GGEMM_VARK_PATH_TCGEN05   1      /* force the tcgen05 CTA-pair path (ELAYOUT if not expressible) */

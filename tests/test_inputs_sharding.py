@@ -131,3 +131,36 @@ def test_two_gloo_ranks_shard_and_gather():
         pr.join(timeout=120)
     assert all(pr.exitcode == 0 for pr in procs)
     assert q.get(timeout=5) is True
+
+
+def _rank_dies_main(rank, world, port, result_q):
+    """Rank 1 leaves before the barrier (as a crashed rank would); rank 0 must get an error from
+    the process-group timeout instead of waiting forever."""
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # no barrier, no destroy: the rank is gone
+    try:
+        dist.barrier()
+        result_q.put("no error")
+    except Exception as e:  # timeout / connection closed
+        result_q.put(type(e).__name__)
+
+
+def test_lost_rank_is_detected_by_the_others():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_rank_dies_main, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=60)
+    alive = [pr for pr in procs if pr.is_alive()]
+    for pr in alive:
+        pr.kill()
+    assert not alive, "a rank hung waiting for the lost rank"
+    assert q.get(timeout=5) != "no error"

@@ -223,8 +223,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const CUtensorMap* gmap_rhs = nullptr;
     bool ok = smid < static_cast<uint32_t>(p.num_sms);
     if (!ok && lane == 0) report_timeout(ctl, 0x500u);
+    Item nxt = decode_item(p, cluster, false);
     for (int item = cluster; item < num_items && ok; item += nclusters) {
-      const Item t = decode_item(p, item, false);
+      const Item t = nxt;  // decoded one item ahead: the offsets' load latency is hidden
+      if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
       if (t.tokens == 0) continue;
       if (t.g != cur_group) {
         slot = (slot + 1) % TMAP_SLOTS;
@@ -301,8 +303,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
+      Item nxt = decode_item(p, cluster, false);
       for (int item = cluster; item < num_items && ok; item += nclusters) {
-        const Item t = decode_item(p, item, false);
+        const Item t = nxt;
+        if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
         if (t.tokens == 0) continue;
         const int nkb = (t.tokens + TK - 1) / TK;
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
@@ -366,8 +370,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       return buf;
     };
+    const bool reporter = leader && ew == 0 && lane == 0;
+    Item nxt = decode_item(p, cluster, reporter);
     for (int item = cluster; item < num_items; item += nclusters) {
-      const Item t = decode_item(p, item, leader && ew == 0 && lane == 0);
+      const Item t = nxt;
+      if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, reporter);
       const int xcol = t.n0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C col
       const bool cols_live = xcol < p.OUT_N;
       const int rows_here = min(t.nrows, p.OUT_M - t.m0);

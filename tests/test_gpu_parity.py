@@ -214,3 +214,56 @@ def test_gate_up_full_size(gate_up_problem):
         got = float(out[g].double().sum())
         mag = float((out[g].double().abs()).sum())
         assert abs(got - expect) <= 1e-3 * mag + 1e-6, (g, got, expect)
+
+
+def _full_size_check(p, n_groups=3):
+    """Kernel over the whole problem; oracle on the smallest and largest non-empty experts and
+    one more; empty experts must be exact zeros; whole-output determinism."""
+    out = vark(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
+    torch.cuda.synchronize()
+    assert _lib.read_status(clear=True) == 0
+    live = [g for g in range(p.G) if p.lens[g] > 0]
+    groups = sorted({min(live, key=lambda g: p.lens[g]), max(live, key=lambda g: p.lens[g]),
+                     live[len(live) // 2]})[:n_groups]
+    cpu = p.to("cpu")
+    _check(cpu, out, groups=groups, label=p.name)
+    for g in range(p.G):
+        if p.lens[g] == 0:
+            assert bool((out[g] == 0).all())
+    again = vark(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
+    torch.cuda.synchronize()
+    assert torch.equal(again, out)
+    return out
+
+
+@pytest.mark.parametrize("name", ["down", "skew"])
+def test_baseline_configs_full_size(name):
+    """BASELINE configs 2 (down_wgrad) and 3 (Zipf routing, 4 empty experts, sizes not multiples
+    of 128, per-expert scales) at full size."""
+    p = inputs.make_problem(name, seed=0, device="cuda")
+    if name == "skew":
+        assert p.lhs_scale.numel() == p.G and int((p.lens == 0).sum()) == 4
+    _full_size_check(p)
+
+
+def test_reference_exponential_routing_full_size():
+    """The reference harness's own routing (bench.py:205-212, seed 42) at the gate_up shape."""
+    lens = inputs.reference_exponential_lens(32, 131072, 42)
+    p = inputs.make_problem("gate_up", seed=0, device="cuda", lens=lens)
+    _full_size_check(p)
+
+
+def test_shard120b_on_one_gpu_and_sharded_equivalence():
+    """BASELINE config 4 (G=128, M_total=1048576, 2880 x 5760) on one GPU, then the same problem
+    computed as 4 expert shards (rebased offsets, token-row slices): bit-identical."""
+    from ggemm_asm_b200 import sharding
+
+    p = inputs.make_problem("shard120b", seed=0, device="cuda")
+    full = _full_size_check(p, n_groups=2)
+    shards = sharding.partition(p.lens, 4)
+    for sh in shards:
+        loc = torch.from_numpy(sharding.local_offsets(p.offs, sh)).to("cuda")
+        part = vark(p.lhs[sh.t_begin:sh.t_end], p.rhs[sh.t_begin:sh.t_end], p.lhs_scale,
+                    p.rhs_scale, loc)
+        torch.cuda.synchronize()
+        assert torch.equal(part, full[sh.g_begin:sh.g_end]), f"shard {sh.rank} differs"

@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config gate_up] [--impl ours|reference]
 
 One step = one call of the hot path over one synthetic batch: every expert's weight gradient
-C[g] = sL*sR * LHS_g^T RHS_g for the configured problem (default: BASELINE config 1,
+C[g] = sL*sR * LHS_g^T RHS_g for the configured problem (default: the gate_up benchmark,
 GPT-OSS-20B gate_up_wgrad: G=32, M_total=131072, 2880 x 5760, e4m3 x e5m2 -> bf16).
 Metric: TFLOPS = 2*M_total*OUT_M*OUT_N / time (launcher.cpp:76), whole job over all GPUs.
 

@@ -1,6 +1,6 @@
 """Generate the committed golden fixtures in this directory. Run from the repository root:
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_CHECKOUT
 
 Outputs
   tiny_seed0.npz             the tiny config (G=4, M_total=1024, 64x128, lens [256,0,512,256])
@@ -64,7 +64,7 @@ def make_reference_lens(ref_root: Path):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference repository")
     args = ap.parse_args()
     make_tiny()
     if Path(args.reference, "bench.py").exists():

@@ -192,7 +192,7 @@ def gate_up_problem():
 
 
 def test_gate_up_full_size(gate_up_problem):
-    """BASELINE config 1 at full size: whole-output cosine against the oracle on 4 experts
+    """The gate_up benchmark problem at full size: whole-output cosine against the oracle on 4 experts
     (incl. the smallest and largest), exact scale linearity, and a checksum identity."""
     p = gate_up_problem
     out = vark(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
@@ -238,7 +238,7 @@ def _full_size_check(p, n_groups=3):
 
 @pytest.mark.parametrize("name", ["down", "skew"])
 def test_baseline_configs_full_size(name):
-    """BASELINE configs 2 (down_wgrad) and 3 (Zipf routing, 4 empty experts, sizes not multiples
+    """The down_wgrad problem and the skewed-routing stress problem (Zipf routing, 4 empty experts, sizes not multiples
     of 128, per-expert scales) at full size."""
     p = inputs.make_problem(name, seed=0, device="cuda")
     if name == "skew":
@@ -254,7 +254,7 @@ def test_reference_exponential_routing_full_size():
 
 
 def test_shard120b_on_one_gpu_and_sharded_equivalence():
-    """BASELINE config 4 (G=128, M_total=1048576, 2880 x 5760) on one GPU, then the same problem
+    """The GPT-OSS-120B-shaped problem (G=128, M_total=1048576, 2880 x 5760) on one GPU, then the same problem
     computed as 4 expert shards (rebased offsets, token-row slices): bit-identical."""
     from ggemm_asm_b200 import sharding
 

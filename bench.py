@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--config", default="gate_up",
                     choices=["gate_up", "down", "skew", "shard120b", "ref_exp"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--op", default="wgrad", choices=["wgrad", "quantize"],
+                    help="wgrad: the grouped GEMM (default, the headline); quantize: the producer "
+                         "step (per-expert amax + fp8 quantisation of x and dy) at the same shape")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -243,10 +246,123 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_quantize(args):
+    """Producer step at the gate_up shape, one GPU: per step, quantise x [M_total, 2880] bf16 ->
+    e4m3 and dy [M_total, 5760] bf16 -> e5m2 with one scale per expert (two launches). Metric:
+    algorithmic HBM bytes per second (2 B read + 1 B written per element; scales and offsets
+    are negligible), against the measured copy bandwidth."""
+    from ggemm_asm_b200 import _lib, inputs, quantize_fp8
+
+    rank, world, local = dist_env()
+    if world != 1:
+        raise SystemExit("--op quantize runs on one GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    cfg = inputs.CONFIGS["gate_up"]
+    lens = inputs.config_lens("gate_up", args.seed)
+    if args.groups is not None or args.tokens is not None:  # smaller case (profiling)
+        lens = inputs.multinomial_lens(args.groups or cfg["G"], args.tokens or cfg["M_total"],
+                                       args.seed)
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens)).to(device)
+    M = int(lens.sum())
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    x = torch.randn(M, cfg["OUT_M"], generator=g, device=device).to(torch.bfloat16)
+    dy = torch.randn(M, cfg["OUT_N"], generator=g, device=device).to(torch.bfloat16)
+    q_x = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=device)
+    q_dy = torch.empty(dy.shape, dtype=torch.float8_e5m2, device=device)
+    s_x = torch.empty(len(lens), dtype=torch.float32, device=device)
+    s_dy = torch.empty_like(s_x)
+    stream = torch.cuda.current_stream(device)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    per_kernel = {"x_e4m3": 0.0, "dy_e5m2": 0.0}
+
+    def step(timed=False):
+        if timed:
+            evs[0].record(stream)
+        quantize_fp8(x, offs, "e4m3", out=q_x, scales=s_x)
+        if timed:
+            evs[1].record(stream)
+        quantize_fp8(dy, offs, "e5m2", out=q_dy, scales=s_dy)
+        if timed:
+            evs[2].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during warm-up")
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    time.sleep(0.05)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    clocks = sampler.window(t0, t1)
+    sampler.__exit__()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    for _ in range(args.steps):  # per-kernel split, separate pass
+        step(timed=True)
+        torch.cuda.synchronize()
+        per_kernel["x_e4m3"] += evs[0].elapsed_time(evs[1]) / args.steps
+        per_kernel["dy_e5m2"] += evs[1].elapsed_time(evs[2]) / args.steps
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during the timed region")
+    bytes_x, bytes_dy = 3 * x.numel(), 3 * dy.numel()
+    value = (bytes_x + bytes_dy) / (ms * 1e-3) / 1e9
+    _fp8, hbm, src = measured_peaks()
+    ach_dy = bytes_dy / (per_kernel["dy_e5m2"] * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": ach_dy, "peak": hbm, "unit": "GB/s",
+                "frac": ach_dy / hbm, "traffic": profile_traffic("quantize_dy_gate_up"),
+                "peak_source": ("of measured: MEASURED_PEAKS.json hbm_gbs (copy, read + write)"
+                                if src.startswith("of measured") else "of fallback: 6.65 TB/s"),
+                "kernel": "vark_quant_tma_kernel<e5m2> (dy, F=5760)",
+                "algorithmic_unit": "3 bytes per element (2 read, 1 written) per launch"}
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import vark_oracle as vo
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        done, secs = 0, 0.0
+        for e in range(len(lens)):
+            lo, hi = int(offs[e]), int(offs[e + 1])
+            xc = dy[lo:hi].cpu()
+            t_s = time.perf_counter()
+            vo.quantize_fp8_ref(xc, [0, hi - lo], "e5m2")
+            secs += time.perf_counter() - t_s
+            done += 3 * xc.numel()
+            if secs > args.cpu_seconds:
+                break
+        cpu = {"value": done / secs / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"dy experts 0..{e} quantised by the torch CPU oracle; "
+                                         f"{secs:.1f} s"}
+    line = {
+        "metric": "producer step (per-expert amax + fp8 quantisation of x and dy) GB/s",
+        "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> fp8 (e4m3 / e5m2)",
+        "data": "synthetic (seeded N(0,1) bf16 on the device)",
+        "config": {"workload": "quantize_gate_up", "G": len(lens), "M_total": M,
+                   "F_x": cfg["OUT_M"], "F_dy": cfg["OUT_N"], "granularity": "group",
+                   "l2": "inputs (2.26 GB) >> 126 MB L2; no flush"},
+        "per_kernel_ms": per_kernel, "e2e": None, "roofline": roofline, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": 2 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.op == "quantize":
+        run_quantize(args)
         return
     rank, world, local = dist_env()
     if world != args.gpus:

@@ -44,6 +44,9 @@ SIGNATURES = {
     "ggemm_vark_fp8_wgrad_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                                     _i32, _i32, _i32, _i32, _i32, _i32, _i64,
                                                     _i32, _vp, _vp]),
+    "ggemm_vark_quantize_workspace_bytes": (ctypes.c_size_t, [_i32]),
+    "ggemm_vark_quantize_fp8": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                                               _i32, _i64, _vp, _vp, _u64, _vp]),
     "ggemm_vark_read_status": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
     "ggemm_vark_tc_supported": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                                                _i32]),

@@ -262,6 +262,26 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
 
 }  // namespace
 
+namespace vark {
+
+// Shared with the other entry points of the library (vark_quant.cu): the current device's status
+// block and SM count, set up on first use.
+int device_status_block(uint32_t** status, int* sm_count) {
+  DeviceState* dev = nullptr;
+  const int rc = get_device(&dev, nullptr);
+  if (rc != GGEMM_VARK_OK) return rc;
+  *status = dev->status;
+  *sm_count = dev->sm_count;
+  return GGEMM_VARK_OK;
+}
+
+int record_cuda_error(cudaError_t e) {
+  cudaGetLastError();
+  return fail_cuda(e);
+}
+
+}  // namespace vark
+
 extern "C" {
 
 int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* c, const float* lhs_scale,

@@ -112,4 +112,13 @@ cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        cudaStream_t stream);
 cudaError_t tc2_set_attributes();
 
+// Library-wide helpers (vark_capi.cu): the current device's status block and SM count (set up
+// on first use; returns a GGEMM_VARK_E* code), and recording of a failed CUDA call for
+// ggemm_vark_last_cuda_error (returns GGEMM_VARK_ECUDA).
+int device_status_block(uint32_t** status, int* sm_count);
+int record_cuda_error(cudaError_t e);
+
+// Workspace bytes of the quantisation kernel (vark_quant.cu) for `units` scaling units.
+size_t quant_workspace_bytes(int32_t units);
+
 }  // namespace vark

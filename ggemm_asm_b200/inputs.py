@@ -154,6 +154,14 @@ def _chunk_normal(rows: int, cols: int, seed: int, chunk: int, which: int, devic
     return x.to(torch.bfloat16)
 
 
+def bf16_source(M_total: int, cols: int, seed: int, which: int, device="cpu") -> torch.Tensor:
+    """The bf16 [M_total, cols] values a problem's operand is quantised from (which: 1 = LHS / x,
+    2 = RHS / dy), generated chunk by chunk exactly as make_problem does."""
+    parts = [_chunk_normal(min(CHUNK_ROWS, M_total - c0), cols, seed, c0 // CHUNK_ROWS, which,
+                           device) for c0 in range(0, M_total, CHUNK_ROWS)]
+    return torch.cat(parts) if parts else torch.empty(0, cols, dtype=torch.bfloat16, device=device)
+
+
 def _row_scale(scales: torch.Tensor, offs: np.ndarray, r0: int, r1: int) -> torch.Tensor:
     """fp32 [r1-r0] scale of each token row."""
     if scales.numel() == 1:

@@ -162,6 +162,37 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs
                             int64_t m_total, int32_t scale_stride,
                             void* status, void* stream);
 
+/*
+ * ggemm_vark_quantize_fp8 - per-expert (or per-tensor) amax scaling and FP8 quantisation of a
+ * token-major bf16 operand: the producer step in front of ggemm_vark_fp8_wgrad (x -> e4m3 LHS,
+ * dy -> e5m2 RHS). No kernel counterpart in the reference: its harness makes the fp8 operands on
+ * the host side (bench.py:221-223, scales fixed by bench.py:266-267).
+ *
+ *  x          bf16 [rows, F], row pitch stride_x elements (2-byte aligned)
+ *  q          fp8 [rows, F], row pitch stride_q bytes; fmt 0: e4m3fn (FMAX 448), 1: e5m2 (57344)
+ *  scales     fp32 [G] (per_group = 1) or [1] (per_group = 0), written by the call
+ *  group_offs device int64 [G + 1]; unit g is rows [off_g, off_{g+1}); per tensor, one unit of
+ *             rows [off_0, off_G)
+ *  m_total    rows allocated in x and q, or -1 if unknown; offsets past it are reported
+ *             (GGEMM_VARK_DEV_BAD_OFFS) and their unit is left unwritten with scale 1.0. With
+ *             m_total == 0, x and q may be NULL.
+ *  workspace  device buffer of ggemm_vark_quantize_workspace_bytes(G) bytes, 16-byte aligned;
+ *             the call clears it on `stream` before the kernel runs (no allocation here)
+ *  status     16-byte aligned status block, or NULL for the library's per-device block
+ *  timeout_ns limit on any single wait of one CTA for the others (0 = default, 2 s)
+ *
+ * Per unit: s = amax/FMAX (fp32 IEEE division; 1.0 for an empty unit or amax == 0; NaN if the
+ * unit holds a NaN), q = fp8(x / s) rounded to nearest even and saturated to +-FMAX. Rows
+ * outside every unit are not written. The kernel is a cooperative launch of one co-resident
+ * grid; calls on different streams must not share a workspace.
+ */
+GGEMM_VARK_API size_t ggemm_vark_quantize_workspace_bytes(int32_t G);
+GGEMM_VARK_API int ggemm_vark_quantize_fp8(const void* x, void* q, float* scales,
+                            const int64_t* group_offs, int32_t G, int32_t F,
+                            int32_t stride_x, int32_t stride_q, int32_t fmt, int32_t per_group,
+                            int64_t m_total, void* workspace, void* status,
+                            uint64_t timeout_ns, void* stream);
+
 /* ggemm_vark_strerror - static description of a GGEMM_VARK_E* code. */
 GGEMM_VARK_API const char* ggemm_vark_strerror(int code);
 

@@ -10,7 +10,10 @@ Reference semantics restated (ggemm-asm):
   * the Triton kernel it is checked against (primus_turbo, not vendored) dequantises with the
     scales and accumulates in fp32.
 
-Three restatements live here:
+The producer step (per-expert amax scaling and fp8 quantisation of x and dy) is restated by
+``quantize_fp8_ref``; the reference harness does this on the host (bench.py:221-223, 266-267).
+
+Three restatements of the wgrad live here:
   ``wgrad_torch``      torch CPU fp32: dequantise each group's slice (fp8 -> fp32, x scale),
                        fp32 matmul, round to bf16 (RNE). This is the parity oracle and the timed
                        CPU baseline.
@@ -160,8 +163,17 @@ def c_lib():
         lib.vark_oracle_wgrad_f64.argtypes = [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_int, ctypes.c_int64,
                                               ctypes.c_int64, vp]
+        lib.vark_oracle_markstein_mismatches.restype = ctypes.c_long
+        lib.vark_oracle_markstein_mismatches.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
         _c = lib
     return _c
+
+
+def markstein_mismatches(lo: int = 0, hi: int = 1 << 23) -> int:
+    """Pairs (bf16 significand a, fp32 divisor b in [1, 2) with bit offsets [lo, hi)) for which
+    the quantiser's division-free quotient differs from IEEE division (plain-C exhaustive check,
+    oracle/vark_oracle_c.c)."""
+    return int(c_lib().vark_oracle_markstein_mismatches(lo, hi))
 
 
 def wgrad_c_f64(lhs, rhs, lhs_scale, rhs_scale, group_offs) -> np.ndarray:
@@ -193,3 +205,33 @@ def closed_form_launcher_value(K: int, scale: float = 0.1) -> float:
     acc = np.float32(K * 0.5)
     v = np.float32(acc * s)
     return float(torch.tensor(float(v), dtype=torch.float32).to(torch.bfloat16).float())
+
+
+FP8_FORMATS = {"e4m3": (torch.float8_e4m3fn, 448.0), "e5m2": (torch.float8_e5m2, 57344.0)}
+
+
+def quantize_fp8_ref(x: torch.Tensor, group_offs, fmt: str, per_group: bool = True):
+    """CPU restatement of the producer step: per unit (expert, or all rows), s = amax|x| / FMAX
+    in fp32 (1.0 for an empty unit or amax 0; NaN when the unit holds a NaN), q = fp8(x / s)
+    with the division in fp32, clamped to +-FMAX, cast round-to-nearest-even.
+
+    Follows the operand construction of the wgrad configurations (amax scaling of N(0,1) bf16,
+    the per-expert variant from the expert's own token slice) and the fp8 cast of the reference
+    harness (bench.py:221-223). Returns (q as uint8 codes [rows, F], rows outside every unit 0;
+    scales fp32 [units]).
+    """
+    dtype, fmax = FP8_FORMATS[fmt]
+    offs = [int(v) for v in (group_offs.tolist() if hasattr(group_offs, "tolist") else group_offs)]
+    units = list(zip(offs[:-1], offs[1:])) if per_group else [(offs[0], offs[-1])]
+    xf = x.float()
+    q = torch.zeros(x.shape, dtype=torch.uint8)
+    scales = torch.ones(len(units), dtype=torch.float32)
+    fmax_t = torch.tensor(fmax, dtype=torch.float32)
+    for u, (lo, hi) in enumerate(units):
+        if hi <= lo:
+            continue
+        amax = xf[lo:hi].abs().amax()
+        s = torch.tensor(1.0) if bool(amax == 0) else amax / fmax_t
+        scales[u] = s
+        q[lo:hi] = (xf[lo:hi] / s).clamp(-fmax, fmax).to(dtype).view(torch.uint8)
+    return q, scales

@@ -89,3 +89,58 @@ int vark_oracle_wgrad_f64(const uint8_t* lhs, const uint8_t* rhs, const float* l
   }
   return 0;
 }
+
+/*
+ * Exhaustive check of the division method the quantiser uses in place of an IEEE division per
+ * element (Markstein's correction step, P. Markstein, "Computation of elementary functions on
+ * the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
+ *     y = RN(1/b),  q = RN(a*y),  r = RN(a - b*q) (one fma, exact),  q' = RN(q + r*y) (one fma)
+ * with a the significand of a bf16 value (k/128, k = 128..255) and b every fp32 in [1, 2).
+ * Every step scales exactly by powers of two while the operands and results stay normal, so
+ * these 2^30 cases stand for all normal a and b. Returns the number of (a, b) with q' != a/b
+ * (the IEEE quotient); the quantiser's tests require 0.
+ */
+#if defined(__x86_64__) && defined(__GNUC__)
+__attribute__((target("fma"))) static long markstein_range_hw(uint32_t lo, uint32_t hi) {
+  long bad = 0;
+  for (uint32_t bits = lo; bits < hi; ++bits) {
+    float b;
+    memcpy(&b, &bits, 4);
+    const float y = 1.0f / b;
+    for (int k = 128; k < 256; ++k) {
+      const float a = (float)k * 0.0078125f;
+      const float q = a * y;
+      const float r = __builtin_fmaf(-b, q, a);
+      const float q2 = __builtin_fmaf(r, y, q);
+      bad += q2 != a / b;
+    }
+  }
+  return bad;
+}
+#endif
+
+static long markstein_range_sw(uint32_t lo, uint32_t hi) {
+  long bad = 0;
+  for (uint32_t bits = lo; bits < hi; ++bits) {
+    float b;
+    memcpy(&b, &bits, 4);
+    const float y = 1.0f / b;
+    for (int k = 128; k < 256; ++k) {
+      const float a = (float)k * 0.0078125f;
+      const float q = a * y;
+      const float r = fmaf(-b, q, a);
+      const float q2 = fmaf(r, y, q);
+      bad += q2 != a / b;
+    }
+  }
+  return bad;
+}
+
+/* Mismatches for b with bit patterns in [0x3f800000 + lo, 0x3f800000 + hi), hi <= 2^23. */
+long vark_oracle_markstein_mismatches(uint32_t lo, uint32_t hi) {
+  if (hi > (1u << 23)) hi = 1u << 23;
+#if defined(__x86_64__) && defined(__GNUC__)
+  if (__builtin_cpu_supports("fma")) return markstein_range_hw(0x3f800000u + lo, 0x3f800000u + hi);
+#endif
+  return markstein_range_sw(0x3f800000u + lo, 0x3f800000u + hi);
+}

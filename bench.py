@@ -51,9 +51,14 @@ def parse():
     ap.add_argument("--config", default="gate_up",
                     choices=["gate_up", "down", "skew", "shard120b", "ref_exp"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="wgrad", choices=["wgrad", "quantize"],
+    ap.add_argument("--op", default="wgrad", choices=["wgrad", "quantize", "fwd"],
                     help="wgrad: the grouped GEMM (default, the headline); quantize: the producer "
-                         "step (per-expert amax + fp8 quantisation of x and dy) at the same shape")
+                         "step (per-expert amax + fp8 quantisation of x and dy) at the same shape; "
+                         "fwd: the fixed-K grouped GEMM of a forward/data-gradient site (--site)")
+    ap.add_argument("--site", default="gate_up_fwd",
+                    choices=["gate_up_fwd", "down_fwd", "down_dgrad", "gate_up_dgrad"],
+                    help="call site of --op fwd (bench.py:154-181 of the reference harness)")
+    ap.add_argument("--no-cublas", action="store_true", help="--op fwd: skip the cuBLAS leg")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -356,6 +361,107 @@ def run_quantize(args):
     print(json.dumps(line), flush=True)
 
 
+FWD_SITES = {  # reference harness bench.py:154-181: (A dtype, N, K); M_total 131072, E 32
+    "gate_up_fwd": ("e4m3", 5760, 2880), "down_fwd": ("e4m3", 2880, 2880),
+    "down_dgrad": ("e5m2", 2880, 2880), "gate_up_dgrad": ("e5m2", 2880, 5760),
+}
+
+
+def run_fwd(args):
+    """Fixed-K grouped GEMM at one harness site on one GPU (reference generator's routing,
+    bench.py:205-212; N(0,1) cast to fp8 and scales 0.1 as bench.py:221-223,257-258). Metric:
+    TFLOPS = 2 * M_total * N * K / time. A per-expert cuBLAS loop (torch._scaled_mm) is timed
+    beside it for context."""
+    from ggemm_asm_b200 import _lib, grouped_gemm_fp8_tensorwise, inputs
+
+    rank, world, local = dist_env()
+    if world != 1:
+        raise SystemExit("--op fwd runs on one GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    a_fmt, N, K = FWD_SITES[args.site]
+    G, M = args.groups or 32, args.tokens or 131072
+    lens = inputs.reference_exponential_lens(G, M, seed=42)
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens)).to(device)
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    a_dtype = torch.float8_e4m3fn if a_fmt == "e4m3" else torch.float8_e5m2
+    a = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16).to(a_dtype)
+    b = torch.randn(G, N, K, generator=g, device=device).to(torch.bfloat16).to(torch.float8_e4m3fn)
+    sa = torch.tensor([0.1], device=device)
+    sb = torch.tensor([0.1], device=device)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during warm-up")
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    time.sleep(0.05)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    clocks = sampler.window(t0, t1)
+    sampler.__exit__()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    flops = 2.0 * M * N * K
+    value = flops / (ms * 1e-3) / 1e12
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during the timed region")
+    cublas = None
+    if not args.no_cublas:
+        # cuBLAS per expert: torch._scaled_mm(a_g, b_g^T) needs row-major A and column-major B;
+        # b[g] is [N, K] row-major, so b[g].t() is column-major [K, N] as required.
+        o = offs.tolist()
+        try:
+            def cub():
+                for e in range(G):
+                    if o[e + 1] > o[e]:
+                        torch._scaled_mm(a[o[e]:o[e + 1]], b[e].t(), scale_a=sa, scale_b=sb,
+                                         out_dtype=torch.bfloat16)
+            for _ in range(3):
+                cub()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(args.steps):
+                cub()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            cms = ev0.elapsed_time(ev1) / args.steps
+            cublas = {"ms": cms, "tflops": flops / (cms * 1e-3) / 1e12,
+                      "what": "torch._scaled_mm per expert (cuBLAS), same data"}
+        except Exception as exc:  # e.g. an fp8 combination cuBLAS does not take
+            cublas = {"unavailable": f"{type(exc).__name__}: {str(exc)[:120]}"}
+    fp8_peak, _hbm, peak_src = measured_peaks()
+    line = {
+        "metric": f"{args.site} fixed-K grouped FP8 GEMM TFLOPS", "value": value, "unit": "TFLOPS",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"fp8({a_fmt} x e4m3) -> fp32 acc -> bf16",
+        "data": "synthetic (N(0,1) cast to fp8, scales 0.1; reference exponential routing)",
+        "config": {"workload": args.site, "G": G, "M_total": M, "N": N, "K": K,
+                   "l2": "operands >> 126 MB L2; no flush"},
+        "roofline": {"bound": "tensor", "achieved": value, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": value / fp8_peak, "peak_source": peak_src,
+                     "frac_of_nominal_4500": value / FP8_NOMINAL_TFLOPS,
+                     "kernel": "vark_fwd2_kernel", "traffic": profile_traffic(args.site)},
+        "cublas_per_expert": cublas, "clocks": clocks, "gpu_launches": args.steps, "e2e": None,
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -363,6 +469,9 @@ def main():
         return
     if args.op == "quantize":
         run_quantize(args)
+        return
+    if args.op == "fwd":
+        run_fwd(args)
         return
     rank, world, local = dist_env()
     if world != args.gpus:

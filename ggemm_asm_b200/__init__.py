@@ -7,6 +7,8 @@ Public API:
                                           ggemm-asm harness makes, bench.py:268)
   variable_k_wgrad                        alias
   launch_raw                              the 14-argument C-ABI drop-in with raw pointers
+  grouped_gemm_fp8_tensorwise             fixed-K grouped GEMM of the forward / data-gradient
+                                          sites (mirrors the Primus-Turbo call, bench.py:260)
   quantize_fp8                            per-expert amax scaling + fp8 quantisation of x / dy
                                           (the producer step in front of the wgrad)
   inputs / sharding                       seeded problems and expert sharding for 1..8 GPUs
@@ -19,6 +21,7 @@ from .grouped_gemm import (  # noqa: F401
     variable_k_wgrad,
 )
 from ._lib import VarkError, read_status  # noqa: F401
+from .grouped_fwd import grouped_gemm_fp8_tensorwise  # noqa: F401
 from .quantize import quantize_fp8  # noqa: F401
 
 __version__ = "0.1.0"

@@ -24,7 +24,7 @@ LIB_PATH = PKG / "libggemm_vark.so"
 LAUNCHER_PATH = PKG / "_build" / "ggemm_vark_launcher"
 
 LIB_SOURCES = ["vark_tc.cu", "vark_tc2.cu", "vark_simt.cu", "vark_capi.cu", "vark_noalloc.cu",
-               "vark_quant.cu"]
+               "vark_quant.cu", "vark_fwd.cu"]
 HEADERS = ["vark_ptx.cuh", "vark_internal.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -69,6 +69,7 @@ int get_device(DeviceState** out, int* dev_out) {
     if (s.cc_major != 10 || s.cc_minor != 0) return GGEMM_VARK_ENO_DEVICE;  // sm_100 only
     if ((e = vark::tc_set_attributes()) != cudaSuccess) return fail_cuda(e);
     if ((e = vark::tc2_set_attributes()) != cudaSuccess) return fail_cuda(e);
+    if ((e = vark::fwd2_set_attributes()) != cudaSuccess) return fail_cuda(e);
     // One allocation per device, kept until exit: the status block and the tensor-map ring.
     void* blk = nullptr;
     const size_t bytes = kStatusBytes + vark::tc_tmap_ring_bytes(kTmapSmIds);
@@ -260,6 +261,95 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
 }
 
+// The fixed-K grouped GEMM (forward / data-gradient sites): argument checks, tensor maps, launch.
+int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const float* b_scale,
+            const int64_t* offs, int32_t G, int32_t N, int32_t K, int32_t sam, int32_t sbg,
+            int32_t sbn, int32_t scm, int32_t scn, int64_t m_total, int32_t a_fmt,
+            int32_t scale_stride, void* status, uint64_t timeout_ns, void* stream) {
+  if (a_scale == nullptr || b_scale == nullptr || offs == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  if (m_total != 0 && (a == nullptr || b == nullptr || c == nullptr)) return GGEMM_VARK_EINVAL_PTR;
+  if (G < 0 || N <= 0 || K <= 0) return GGEMM_VARK_EINVAL_SHAPE;
+  if (sam < K || sbn < K || scn <= 0 || scm < N ||
+      static_cast<int64_t>(sbg) < static_cast<int64_t>(N - 1) * sbn + K)
+    return GGEMM_VARK_EINVAL_STRIDE;
+  if ((a_fmt != 0 && a_fmt != 1) || (scale_stride != 0 && scale_stride != 1) || m_total < -1)
+    return GGEMM_VARK_EINVAL_ARG;
+  if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
+  if (a != nullptr && (!aligned16(a) || !aligned16(b) || !aligned16(c) || sam % 16 != 0 ||
+                       sbn % 16 != 0 || sbg % 16 != 0 || scn != 1 || (2ll * scm) % 16 != 0))
+    return GGEMM_VARK_ELAYOUT;
+  if (G == 0 || m_total == 0) return GGEMM_VARK_OK;
+
+  DeviceState* dev = nullptr;
+  int rc = get_device(&dev, nullptr);
+  if (rc != GGEMM_VARK_OK) return rc;
+  if (dev->sm_count < 2) return GGEMM_VARK_ENO_DEVICE;
+  const int64_t token_limit =
+      m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
+
+  // A [rows, K] u8 and C [rows, N] bf16: the kernel replaces base and row extent per expert.
+  CUtensorMap map_a, map_b, map_c;
+  const uint64_t rows = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(sam)};
+    const cuuint32_t box[2] = {128, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    if (g_encode(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return GGEMM_VARK_ELAYOUT;
+  }
+  {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N),
+                                static_cast<cuuint64_t>(G)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(sbn), static_cast<cuuint64_t>(sbg)};
+    const cuuint32_t box[3] = {128, 128, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (g_encode(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(b), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return GGEMM_VARK_ELAYOUT;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), rows};
+    const cuuint64_t strides[1] = {2ull * static_cast<cuuint64_t>(scm)};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    if (g_encode(&map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return GGEMM_VARK_ELAYOUT;
+  }
+  vark::FwdParams fp;
+  fp.group_offs = offs;
+  fp.a_scale = a_scale;
+  fp.b_scale = b_scale;
+  fp.b_scale_stride = scale_stride;
+  fp.G = G;
+  fp.N = N;
+  fp.K = K;
+  fp.n_tiles = (N + 255) / 256;
+  fp.a_fmt = a_fmt;
+  fp.token_limit = token_limit;
+  fp.status = status != nullptr ? static_cast<uint32_t*>(status) : dev->status;
+  fp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
+  fp.a = static_cast<const uint8_t*>(a);
+  fp.stride_am = sam;
+  fp.c = static_cast<uint16_t*>(c);
+  fp.stride_cm = scm;
+  fp.tmap_ring = dev->tmap_ring;
+  fp.num_sms = kTmapSmIds;
+  // The item count depends on the group sizes, which stay on the device: one cluster per pair
+  // of SMs, each walking the items round-robin (clusters without items exit at once).
+  const cudaError_t e = vark::fwd2_launch(map_a, map_b, map_c, fp, 2 * (dev->sm_count / 2),
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
+}
+
 }  // namespace
 
 namespace vark {
@@ -303,6 +393,26 @@ int ggemm_vark_fp8_wgrad_ex(const void* lhs, const void* rhs, void* c, const flo
   return run(lhs, rhs, c, lhs_scale, rhs_scale, group_offs, G, OUT_M, OUT_N, stride_lhs_m,
              stride_rhs_m, stride_cg, stride_cm, stride_cn, m_total, scale_stride, path, status,
              timeout_ns, stream);
+}
+
+int ggemm_vark_grouped_fp8_fwd(const void* a, const void* b, void* c, const float* a_scale,
+                               const float* b_scale, const int64_t* group_offs, int32_t G,
+                               int32_t N, int32_t K, int32_t stride_am, int32_t stride_bg,
+                               int32_t stride_bn, int32_t stride_cm, int32_t stride_cn,
+                               void* stream) {
+  return run_fwd(a, b, c, a_scale, b_scale, group_offs, G, N, K, stride_am, stride_bg, stride_bn,
+                 stride_cm, stride_cn, /*m_total=*/-1, /*a_fmt=*/0, /*scale_stride=*/0,
+                 /*status=*/nullptr, /*timeout_ns=*/0, stream);
+}
+
+int ggemm_vark_grouped_fp8_fwd_ex(const void* a, const void* b, void* c, const float* a_scale,
+                                  const float* b_scale, const int64_t* group_offs, int32_t G,
+                                  int32_t N, int32_t K, int32_t stride_am, int32_t stride_bg,
+                                  int32_t stride_bn, int32_t stride_cm, int32_t stride_cn,
+                                  int64_t m_total, int32_t a_fmt, int32_t scale_stride,
+                                  void* status, uint64_t timeout_ns, void* stream) {
+  return run_fwd(a, b, c, a_scale, b_scale, group_offs, G, N, K, stride_am, stride_bg, stride_bn,
+                 stride_cm, stride_cn, m_total, a_fmt, scale_stride, status, timeout_ns, stream);
 }
 
 int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out) {

@@ -112,6 +112,34 @@ cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        cudaStream_t stream);
 cudaError_t tc2_set_attributes();
 
+// Fixed-K grouped GEMM (vark_fwd.cu): C[t, :] = sA * sB_g * A[t, :] . B[g]^T for the tokens t of
+// expert g; A [tokens, K] and B [G, N, K] are K-major fp8, C bf16. Tensor maps (encoded by the
+// caller): A 2D u8 {K, rows} box {128, 128}; B 3D u8 {K, N, G} box {128, 128, 1}; C 2D bf16
+// {N, rows} box {32, 32} with the 64-byte swizzle. The kernel rebuilds the A and C maps per expert.
+struct FwdParams {
+  const int64_t* group_offs;
+  const float* a_scale;   // one value
+  const float* b_scale;   // one value, or G values when b_scale_stride == 1
+  int32_t b_scale_stride;
+  int32_t G, N, K;
+  int32_t n_tiles;        // ceil(N / 256)
+  int32_t a_fmt;          // 0: e4m3, 1: e5m2 (B is e4m3)
+  int64_t token_limit;    // group offsets above this are invalid
+  uint32_t* status;
+  uint64_t timeout_ns;
+  const uint8_t* a;       // A base; row pitch in bytes
+  int64_t stride_am;
+  uint16_t* c;            // C base (bf16 bits); row pitch in elements
+  int64_t stride_cm;
+  uint8_t* tmap_ring;     // as TcParams::tmap_ring
+  int32_t num_sms;
+};
+size_t fwd2_smem_bytes();
+cudaError_t fwd2_launch(const CUtensorMap& map_a, const CUtensorMap& map_b,
+                        const CUtensorMap& map_c, const FwdParams& p, int grid,
+                        cudaStream_t stream);
+cudaError_t fwd2_set_attributes();
+
 // Library-wide helpers (vark_capi.cu): the current device's status block and SM count (set up
 // on first use; returns a GGEMM_VARK_E* code), and recording of a failed CUDA call for
 // ggemm_vark_last_cuda_error (returns GGEMM_VARK_ECUDA).

@@ -163,6 +163,45 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs
                             void* status, void* stream);
 
 /*
+ * ggemm_vark_grouped_fp8_fwd - the fixed-K grouped FP8 GEMM of the MoE forward and data-gradient
+ * sites (the harness's "persistent" kernel type, ggemm-asm bench.py:154-181, launched with the
+ * argument layout of bench.py:312-338; the reference ships no kernel for it, its harness runs
+ * Primus-Turbo's grouped_gemm_fp8_tensorwise_triton_kernel, bench.py:241-260):
+ *
+ *     C[t, n] = a_scale * b_scale * sum_k A[t, k] * B[g, n, k]   for off_g <= t < off_{g+1}
+ *
+ *  A          [rows, K] float8 e4m3fn (this entry point) with row pitch stride_am (elements =
+ *             bytes); K contiguous
+ *  B          [G, N, K] float8 e4m3fn ("trans_b"): expert stride stride_bg, row stride stride_bn
+ *  C          [rows, N] bf16, row pitch stride_cm, stride_cn == 1; rows of every expert are
+ *             overwritten, other rows are not touched
+ *  scales     device fp32 scalars; group_offs device int64 [G + 1]
+ * Tensor-core layout rules: 16-byte aligned bases; stride_am, stride_bn, stride_bg and
+ * 2 * stride_cm multiples of 16; stride_cn == 1 (GGEMM_VARK_ELAYOUT otherwise). Like the
+ * 14-argument wgrad entry point it trusts group_offs to lie inside A and C.
+ */
+GGEMM_VARK_API int ggemm_vark_grouped_fp8_fwd(const void* a, const void* b, void* c,
+                            const float* a_scale, const float* b_scale,
+                            const int64_t* group_offs, int32_t G, int32_t N, int32_t K,
+                            int32_t stride_am, int32_t stride_bg, int32_t stride_bn,
+                            int32_t stride_cm, int32_t stride_cn, void* stream);
+
+/*
+ * ggemm_vark_grouped_fp8_fwd_ex - the same with the A format selectable and the extensions of
+ * ggemm_vark_fp8_wgrad_ex: m_total (rows allocated in A and C, or -1; offsets past it are
+ * reported and their expert skipped; 0 allows NULL a, b, c), a_fmt (0: e4m3fn for the forward
+ * sites, 1: e5m2 for the data-gradient sites; B stays e4m3fn), scale_stride (0: one b_scale,
+ * 1: G per-expert b_scale values; a_scale is always one value), status and timeout_ns.
+ */
+GGEMM_VARK_API int ggemm_vark_grouped_fp8_fwd_ex(const void* a, const void* b, void* c,
+                            const float* a_scale, const float* b_scale,
+                            const int64_t* group_offs, int32_t G, int32_t N, int32_t K,
+                            int32_t stride_am, int32_t stride_bg, int32_t stride_bn,
+                            int32_t stride_cm, int32_t stride_cn, int64_t m_total,
+                            int32_t a_fmt, int32_t scale_stride, void* status,
+                            uint64_t timeout_ns, void* stream);
+
+/*
  * ggemm_vark_quantize_fp8 - per-expert (or per-tensor) amax scaling and FP8 quantisation of a
  * token-major bf16 operand: the producer step in front of ggemm_vark_fp8_wgrad (x -> e4m3 LHS,
  * dy -> e5m2 RHS). No kernel counterpart in the reference: its harness makes the fp8 operands on

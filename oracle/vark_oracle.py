@@ -235,3 +235,39 @@ def quantize_fp8_ref(x: torch.Tensor, group_offs, fmt: str, per_group: bool = Tr
         scales[u] = s
         q[lo:hi] = (xf[lo:hi] / s).clamp(-fmax, fmax).to(dtype).view(torch.uint8)
     return q, scales
+
+
+def grouped_fwd_f32(a: torch.Tensor, b: torch.Tensor, a_scale, b_scale, group_offs,
+                    rows=None) -> torch.Tensor:
+    """CPU restatement of the fixed-K grouped GEMM (the harness's persistent sites, bench.py:
+    154-181, checked there against Primus-Turbo's grouped_gemm_fp8_tensorwise_triton_kernel,
+    bench.py:260): per expert g, out[off_g:off_{g+1}] = sA * sB_g * a_g @ b[g]^T, fp8 decoded to
+    fp32, fp32 matmul. Returns fp32 [M, N]; `rows` (optional index tensor) restricts the output
+    to those token rows (returned in that order)."""
+    offs = [int(v) for v in (group_offs.tolist() if hasattr(group_offs, "tolist") else group_offs)]
+    G, N, _ = b.shape
+    sa = float(a_scale.reshape(-1)[0])
+    sb = b_scale.reshape(-1).float()
+    which = torch.arange(a.shape[0]) if rows is None else torch.as_tensor(rows)
+    out = torch.zeros(which.numel(), N, dtype=torch.float32)
+    starts = torch.tensor(offs[:-1])
+    ends = torch.tensor(offs[1:])
+    gid = torch.searchsorted(torch.tensor(offs[1:]), which, right=True)
+    for g in range(G):
+        sel = ((gid == g) & (which >= starts[g]) & (which < ends[g])).nonzero().flatten()
+        if sel.numel() == 0:
+            continue
+        ag = a[which[sel]].float()
+        bg = b[g].float()
+        s = sa * float(sb[g] if sb.numel() > 1 else sb[0])
+        out[sel] = (ag @ bg.T) * s
+    return out
+
+
+def grouped_fwd_tolerance(a, b, a_scale, b_scale, group_offs, ref: torch.Tensor, rows=None):
+    """|C - ref| bound: one bf16 ulp of |ref| plus fp32 reassociation over K terms,
+    K * 2^-24 * sA * sB * (|a| @ |b|^T) (the same form as the wgrad's)."""
+    K = a.shape[1]
+    absd = grouped_fwd_f32(_abs_fp8(a), _abs_fp8(b), a_scale.abs(), b_scale.abs(), group_offs,
+                           rows)
+    return bf16_ulp(ref.abs()) + K * 2.0 ** -24 * absd

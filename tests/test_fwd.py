@@ -1,0 +1,254 @@
+"""The fixed-K grouped FP8 GEMM (forward / data-gradient sites): oracle pins and C-ABI rules on
+the CPU, parity with the oracle on the GPU (ragged experts, edge tiles in N, K tails, both A
+formats, per-expert scales, rows outside the experts untouched, the harness's full-size sites)."""
+import numpy as np
+import pytest
+import torch
+
+from ggemm_asm_b200 import _lib, grouped_gemm_fp8_tensorwise, inputs
+from oracle import vark_oracle as vo
+
+P = 1 << 20  # fake aligned device address: never dereferenced by the CPU tests
+E4M3, E5M2 = torch.float8_e4m3fn, torch.float8_e5m2
+
+
+def make_fwd(lens, N, K, a_dtype=E4M3, seed=0, per_expert_scale=False):
+    """Seeded problem: a [M, K] (N(0,1) cast to fp8 as bench.py:221-223 does), b [G, N, K]
+    e4m3, scales 0.1 (bench.py:257-258) or per-expert values."""
+    g = torch.Generator().manual_seed(seed)
+    M, G = int(sum(lens)), len(lens)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(a_dtype)
+    b = torch.randn(G, N, K, generator=g).to(torch.bfloat16).to(E4M3)
+    sa = torch.tensor([0.1], dtype=torch.float32)
+    sb = (torch.rand(G, generator=g) * 0.2 + 0.05) if per_expert_scale else torch.tensor([0.1])
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens))
+    return a, b, sa, sb.float(), offs
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU
+# ------------------------------------------------------------------------------------------------
+def test_oracle_matches_float64_restatement():
+    a, b, sa, sb, offs = make_fwd([5, 0, 17, 3], N=24, K=40, a_dtype=E5M2, per_expert_scale=True)
+    ref = vo.grouped_fwd_f32(a, b, sa, sb, offs)
+    ta = vo.fp8_decode_table("e5m2")[a.view(torch.uint8).numpy()]
+    tb = vo.fp8_decode_table("e4m3fn")[b.view(torch.uint8).numpy()]
+    exact = np.zeros((a.shape[0], 24))
+    o = offs.tolist()
+    for gi in range(4):
+        exact[o[gi]:o[gi + 1]] = ta[o[gi]:o[gi + 1]] @ tb[gi].T * 0.1 * float(sb[gi])
+    tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref)
+    assert (np.abs(ref.numpy() - exact) <= tol.numpy()).all()
+    assert float(np.abs(exact).max()) > 0
+
+
+def test_oracle_row_subset():
+    a, b, sa, sb, offs = make_fwd([7, 0, 9], N=16, K=32)
+    full = vo.grouped_fwd_f32(a, b, sa, sb, offs)
+    rows = torch.tensor([15, 0, 8, 6])
+    assert torch.equal(vo.grouped_fwd_f32(a, b, sa, sb, offs, rows), full[rows])
+
+
+def call_fwd(**kw):
+    x = dict(a=P, b=P, c=P, sa=P, sb=P, offs=P, G=4, N=256, K=512, sam=512, sbg=256 * 512,
+             sbn=512, scm=256, scn=1, m=1024, fmt=0, ss=0, status=None)
+    x.update(kw)
+    return _lib.lib().ggemm_vark_grouped_fp8_fwd_ex(
+        x["a"], x["b"], x["c"], x["sa"], x["sb"], x["offs"], x["G"], x["N"], x["K"], x["sam"],
+        x["sbg"], x["sbn"], x["scm"], x["scn"], x["m"], x["fmt"], x["ss"], x["status"], 0, None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(sa=None), _lib.EINVAL_PTR), (dict(offs=None), _lib.EINVAL_PTR),
+    (dict(a=None), _lib.EINVAL_PTR), (dict(c=None), _lib.EINVAL_PTR),
+    (dict(G=-1), _lib.EINVAL_SHAPE), (dict(N=0), _lib.EINVAL_SHAPE), (dict(K=0), _lib.EINVAL_SHAPE),
+    (dict(sam=500), _lib.EINVAL_STRIDE), (dict(sbn=100), _lib.EINVAL_STRIDE),
+    (dict(sbg=1000), _lib.EINVAL_STRIDE), (dict(scm=100), _lib.EINVAL_STRIDE),
+    (dict(scn=0), _lib.EINVAL_STRIDE),
+    (dict(fmt=2), _lib.EINVAL_ARG), (dict(ss=2), _lib.EINVAL_ARG), (dict(m=-2), _lib.EINVAL_ARG),
+    (dict(status=P + 4), _lib.EINVAL_ARG),
+    (dict(a=P + 8), _lib.ELAYOUT), (dict(sam=520), _lib.ELAYOUT), (dict(scn=2), _lib.ELAYOUT),
+    (dict(scm=260), _lib.ELAYOUT), (dict(sbn=520, sbg=256 * 520), _lib.ELAYOUT),
+    (dict(G=0), _lib.OK), (dict(m=0, a=None, b=None, c=None), _lib.OK),
+])
+def test_fwd_argument_checks(kw, code):
+    assert call_fwd(**kw) == code
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device answer")
+def test_fwd_without_device():
+    assert call_fwd() == _lib.ENO_DEVICE
+    assert _lib.lib().ggemm_vark_grouped_fp8_fwd(P, P, P, P, P, P, 4, 256, 512, 512, 256 * 512,
+                                                 512, 256, 1, None) == _lib.ENO_DEVICE
+
+
+def test_torch_fwd_validates_before_launch():
+    a, b, sa, sb, offs = make_fwd([4, 4], N=16, K=32)
+    with pytest.raises(ValueError, match="CUDA"):
+        grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs)
+    with pytest.raises(NotImplementedError):
+        grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs, trans_b=False)
+    with pytest.raises(TypeError):
+        grouped_gemm_fp8_tensorwise(a, b.view(E5M2), sa, sb, offs)
+    with pytest.raises(ValueError, match="G\\+1"):
+        grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs[:-1])
+    with pytest.raises(ValueError, match="b_scale"):
+        grouped_gemm_fp8_tensorwise(a, b, sa, torch.ones(3), offs)
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU
+# ------------------------------------------------------------------------------------------------
+def run_gpu(a, b, sa, sb, offs, out=None, status=None):
+    return grouped_gemm_fp8_tensorwise(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), offs.cuda(),
+                                       out=out, status=status)
+
+
+def check(a, b, sa, sb, offs, got, rows=None):
+    ref = vo.grouped_fwd_f32(a, b, sa, sb, offs, rows)
+    tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref, rows)
+    g = got.float().cpu() if rows is None else got.float().cpu()[rows]
+    err = (g - ref).abs()
+    assert bool((err <= tol).all()), f"max excess {float((err - tol).max())}"
+    if ref.abs().max() > 0:
+        assert vo.cosine(g, ref) >= 0.99999
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("a_dtype", [E4M3, E5M2])
+@pytest.mark.parametrize("lens,N,K", [
+    ([256], 256, 256),                      # one full tile, one full stage
+    ([300, 0, 77, 1, 511], 320, 288),       # ragged experts, N edge 64, K tail 32
+    ([1000, 24], 48, 96),                   # N < 256, K < 256
+    ([129, 700], 2880, 2880),               # the down sites' N and K (tails 64 and 64)
+    ([513], 16, 32),                        # smallest N and K
+    ([40] * 40, 272, 128),                  # many small experts, N edge 16
+])
+def test_fwd_matches_oracle(a_dtype, lens, N, K):
+    a, b, sa, sb, offs = make_fwd(lens, N, K, a_dtype, seed=N + K)
+    got = run_gpu(a, b, sa, sb, offs)
+    torch.cuda.synchronize()
+    check(a, b, sa, sb, offs, got)
+
+
+@pytest.mark.gpu
+def test_fwd_per_expert_scales_and_status():
+    a, b, sa, sb, offs = make_fwd([300, 0, 200, 57], 384, 640, E5M2, seed=3, per_expert_scale=True)
+    status = torch.zeros(64, dtype=torch.int32, device="cuda")
+    got = run_gpu(a, b, sa, sb, offs, status=status)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 0
+    check(a, b, sa, sb, offs, got)
+
+
+@pytest.mark.gpu
+def test_fwd_rows_outside_experts_untouched():
+    """offs[0] > 0 and offs[G] < M: only the experts' rows are written (C store clipped per
+    expert), so the sentinel survives elsewhere - including right after a partial token tile."""
+    a, b, sa, sb, _ = make_fwd([1100], 256, 256, seed=5)
+    offs = torch.tensor([50, 300, 300, 1000], dtype=torch.int64)
+    b3 = torch.cat([b, b, b])
+    out = torch.full((1100, 256), 7.0, dtype=torch.bfloat16, device="cuda")
+    run_gpu(a, b3, sa, sb, offs, out=out)
+    torch.cuda.synchronize()
+    o = out.cpu()
+    assert bool((o[:50] == 7).all()) and bool((o[1000:] == 7).all())
+    rows = torch.arange(50, 1000)
+    check(a, b3, sa, sb, offs, o, rows)
+
+
+@pytest.mark.gpu
+def test_fwd_padded_strides_and_14_arg_entry():
+    lens, N, K = [333, 222], 272, 320
+    a, b, sa, sb, offs = make_fwd(lens, N, K, seed=9)
+    ap = torch.zeros(a.shape[0], K + 64, dtype=torch.uint8)
+    ap[:, :K] = a.view(torch.uint8)
+    bp = torch.zeros(2, N + 8, K + 32, dtype=torch.uint8)
+    bp[:, :N, :K] = b.view(torch.uint8)
+    ad = ap.cuda().view(E4M3)[:, :K]
+    bd = bp.cuda().view(E4M3)[:, :N, :K]
+    out = torch.zeros(a.shape[0], N + 8, dtype=torch.bfloat16, device="cuda")[:, :N]
+    grouped_gemm_fp8_tensorwise(ad, bd, sa.cuda(), sb.cuda(), offs.cuda(), out=out)
+    torch.cuda.synchronize()
+    check(a, b, sa, sb, offs, out)
+    out2 = torch.zeros_like(out)
+    sa_d, sb_d, offs_d = sa.cuda(), sb.cuda(), offs.cuda()
+    rc = _lib.lib().ggemm_vark_grouped_fp8_fwd(
+        ad.data_ptr(), bd.data_ptr(), out2.data_ptr(), sa_d.data_ptr(), sb_d.data_ptr(),
+        offs_d.data_ptr(), 2, N, K, ad.stride(0), bd.stride(0), bd.stride(1), out2.stride(0), 1,
+        torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.OK
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+
+
+@pytest.mark.gpu
+def test_fwd_deterministic():
+    a, b, sa, sb, offs = make_fwd([900, 5, 400], 512, 512, seed=11)
+    x = run_gpu(a, b, sa, sb, offs)
+    y = run_gpu(a, b, sa, sb, offs)
+    torch.cuda.synchronize()
+    assert torch.equal(x, y)
+
+
+@pytest.mark.gpu
+def test_fwd_bad_offsets_reported():
+    a, b, sa, sb, offs = make_fwd([100, 100], 64, 64, seed=2)
+    bad = torch.tensor([0, 150, 120], dtype=torch.int64)
+    status = torch.zeros(64, dtype=torch.int32, device="cuda")
+    run_gpu(a, b, sa, sb, bad, status=status)
+    torch.cuda.synchronize()
+    assert int(status[0]) & _lib.DEV_BAD_OFFS
+
+
+@pytest.mark.gpu
+def test_fwd_expired_wait_is_reported():
+    import time
+
+    a, b, sa, sb, offs = make_fwd([600, 300], 512, 512, seed=4)
+    status = torch.zeros(64, dtype=torch.int32, device="cuda")
+    status[3] = 0x5374616C
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    grouped_gemm_fp8_tensorwise(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), offs.cuda(),
+                                status=status, timeout_ns=20_000_000)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(status[0]) & _lib.DEV_TIMEOUT
+    got = run_gpu(a, b, sa, sb, offs)
+    torch.cuda.synchronize()
+    check(a, b, sa, sb, offs, got)
+
+
+SITES = {  # bench.py:154-181 (M_total = 131072, E = 32)
+    "gate_up_fwd": (E4M3, 5760, 2880), "down_fwd": (E4M3, 2880, 2880),
+    "down_dgrad": (E5M2, 2880, 2880), "gate_up_dgrad": (E5M2, 2880, 5760),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("site", sorted(SITES))
+def test_fwd_full_size_site(site):
+    """Full-size harness site with the reference generator's routing: 8 rows of every expert
+    (first, last and random ones) against the CPU oracle, plus a determinism check."""
+    a_dtype, N, K = SITES[site]
+    lens = inputs.reference_exponential_lens(32, 131072, seed=42)
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens))
+    g = torch.Generator(device="cuda").manual_seed(N + K)
+    a = torch.randn(131072, K, generator=g, device="cuda").to(torch.bfloat16).to(a_dtype)
+    b = torch.randn(32, N, K, generator=g, device="cuda").to(torch.bfloat16).to(E4M3)
+    sa = torch.tensor([0.1], device="cuda")
+    sb = torch.tensor([0.1], device="cuda")
+    out = grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs.cuda())
+    torch.cuda.synchronize()
+    o = offs.tolist()
+    rng = np.random.default_rng(0)
+    rows = []
+    for e in range(32):
+        if o[e + 1] > o[e]:
+            rows += [o[e], o[e + 1] - 1] + list(rng.integers(o[e], o[e + 1], 6))
+    rows = torch.tensor(sorted(set(rows)))
+    check(a.cpu(), b.cpu(), sa.cpu(), sb.cpu(), offs, out, rows)
+    again = grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)

@@ -51,10 +51,11 @@ def parse():
     ap.add_argument("--config", default="gate_up",
                     choices=["gate_up", "down", "skew", "shard120b", "ref_exp"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="wgrad", choices=["wgrad", "quantize", "fwd"],
+    ap.add_argument("--op", default="wgrad", choices=["wgrad", "quantize", "fwd", "layer"],
                     help="wgrad: the grouped GEMM (default, the headline); quantize: the producer "
                          "step (per-expert amax + fp8 quantisation of x and dy) at the same shape; "
-                         "fwd: the fixed-K grouped GEMM of a forward/data-gradient site (--site)")
+                         "fwd: the fixed-K grouped GEMM of a forward/data-gradient site (--site); "
+                         "layer: one forward + backward step of the FP8 MoE linear layer")
     ap.add_argument("--site", default="gate_up_fwd",
                     choices=["gate_up_fwd", "down_fwd", "down_dgrad", "gate_up_dgrad"],
                     help="call site of --op fwd (bench.py:154-181 of the reference harness)")
@@ -462,6 +463,99 @@ def run_fwd(args):
     print(json.dumps(line), flush=True)
 
 
+def run_layer(args):
+    """One training step (forward + backward) of the FP8 MoE expert linear layer at the gate_up
+    shape (x [131072, 2880], W [32, 2880, 5760], multinomial routing): quantise x and W, forward
+    GEMM, quantise dy, data-gradient GEMM, weight-gradient GEMM. Metric: TFLOPS of the three
+    GEMMs (3 * 2*M*K*N) over the whole step. A bf16 per-expert torch (cuBLAS) loop of the same
+    three products is timed beside it for context."""
+    from ggemm_asm_b200 import _lib, inputs
+    from ggemm_asm_b200.moe import grouped_linear_fp8
+
+    rank, world, local = dist_env()
+    if world != 1:
+        raise SystemExit("--op layer runs on one GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    cfg = inputs.CONFIGS["gate_up"]
+    G, M, K, N = cfg["G"], cfg["M_total"], cfg["OUT_M"], cfg["OUT_N"]
+    lens = inputs.config_lens("gate_up", args.seed)
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens)).to(device)
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    x = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(G, K, N, generator=g, device=device) * K ** -0.5).to(torch.bfloat16)
+    w.requires_grad_(True)
+    dy = torch.randn(M, N, generator=g, device=device).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        x.grad = None
+        w.grad = None
+        y = grouped_linear_fp8(x, w, offs)
+        y.backward(dy)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during warm-up")
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    time.sleep(0.05)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.window(t0, time.perf_counter())
+    sampler.__exit__()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    flops = 3 * 2.0 * M * K * N
+    value = flops / (ms * 1e-3) / 1e12
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during the timed region")
+    bf16 = None
+    if not args.no_cublas:
+        o = offs.tolist()
+        xs = x.detach()
+        ws = w.detach()
+
+        def ref_step():
+            for e in range(G):
+                if o[e + 1] > o[e]:
+                    xe, de = xs[o[e]:o[e + 1]], dy[o[e]:o[e + 1]]
+                    torch.matmul(xe, ws[e])
+                    torch.matmul(de, ws[e].t())
+                    torch.matmul(xe.t(), de)
+        for _ in range(2):
+            ref_step()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(max(2, args.steps // 4)):
+            ref_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        bms = ev0.elapsed_time(ev1) / max(2, args.steps // 4)
+        bf16 = {"ms": bms, "tflops": flops / (bms * 1e-3) / 1e12,
+                "what": "bf16 torch.matmul per expert (cuBLAS): forward, dx, dW; no quantisation"}
+    fp8_peak, _hbm, peak_src = measured_peaks()
+    print(json.dumps({
+        "metric": "FP8 MoE linear layer training step (fwd + dx + dW) TFLOPS", "value": value,
+        "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8 (e4m3 x, W; e5m2 dy) -> fp32 acc -> bf16, per-expert amax scales",
+        "data": "synthetic (seeded N(0,1) bf16 x, dy; W ~ N(0, 1/K))",
+        "config": {"workload": "moe_linear_gate_up", "G": G, "M_total": M, "K": K, "N": N},
+        "roofline": {"bound": "tensor", "achieved": value, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": value / fp8_peak, "peak_source": peak_src,
+                     "note": "includes the three quantisation passes (HBM bound)"},
+        "bf16_cublas_per_expert": bf16, "clocks": clocks, "e2e": None, "cpu_baseline": None,
+    }), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -472,6 +566,9 @@ def main():
         return
     if args.op == "fwd":
         run_fwd(args)
+        return
+    if args.op == "layer":
+        run_layer(args)
         return
     rank, world, local = dist_env()
     if world != args.gpus:

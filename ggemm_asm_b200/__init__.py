@@ -11,6 +11,8 @@ Public API:
                                           sites (mirrors the Primus-Turbo call, bench.py:260)
   quantize_fp8                            per-expert amax scaling + fp8 quantisation of x / dy
                                           (the producer step in front of the wgrad)
+  moe.GroupedLinearFP8 / grouped_linear_fp8  FP8 MoE expert linear layer with autograd (forward,
+                                          data gradient and weight gradient on these kernels)
   inputs / sharding                       seeded problems and expert sharding for 1..8 GPUs
 The C ABI itself is declared in include/ggemm_vark.h and lives in libggemm_vark.so.
 """

@@ -48,7 +48,7 @@ SIGNATURES = {
                                                   _i32, _i32, _i32, _i32, _i32, _vp]),
     "ggemm_vark_grouped_fp8_fwd_ex": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                                      _i32, _i32, _i32, _i32, _i32, _i32, _i64,
-                                                     _i32, _i32, _vp, _u64, _vp]),
+                                                     _i32, _i32, _i32, _vp, _u64, _vp]),
     "ggemm_vark_quantize_workspace_bytes": (ctypes.c_size_t, [_i32]),
     "ggemm_vark_quantize_fp8": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                                _i32, _i64, _vp, _vp, _u64, _vp]),

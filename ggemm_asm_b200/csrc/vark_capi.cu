@@ -265,12 +265,16 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
 int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const float* b_scale,
             const int64_t* offs, int32_t G, int32_t N, int32_t K, int32_t sam, int32_t sbg,
             int32_t sbn, int32_t scm, int32_t scn, int64_t m_total, int32_t a_fmt,
-            int32_t scale_stride, void* status, uint64_t timeout_ns, void* stream) {
+            int32_t scale_stride, int32_t b_layout, void* status, uint64_t timeout_ns,
+            void* stream) {
   if (a_scale == nullptr || b_scale == nullptr || offs == nullptr) return GGEMM_VARK_EINVAL_PTR;
   if (m_total != 0 && (a == nullptr || b == nullptr || c == nullptr)) return GGEMM_VARK_EINVAL_PTR;
   if (G < 0 || N <= 0 || K <= 0) return GGEMM_VARK_EINVAL_SHAPE;
-  if (sam < K || sbn < K || scn <= 0 || scm < N ||
-      static_cast<int64_t>(sbg) < static_cast<int64_t>(N - 1) * sbn + K)
+  if (b_layout != 0 && b_layout != 1) return GGEMM_VARK_EINVAL_ARG;
+  // B rows: N rows of K (layout 0) or K rows of N (layout 1), stride_bn apart.
+  const int32_t b_rows = b_layout == 0 ? N : K, b_row = b_layout == 0 ? K : N;
+  if (sam < K || sbn < b_row || scn <= 0 || scm < N ||
+      static_cast<int64_t>(sbg) < static_cast<int64_t>(b_rows - 1) * sbn + b_row)
     return GGEMM_VARK_EINVAL_STRIDE;
   if ((a_fmt != 0 && a_fmt != 1) || (scale_stride != 0 && scale_stride != 1) || m_total < -1)
     return GGEMM_VARK_EINVAL_ARG;
@@ -302,10 +306,10 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
       return GGEMM_VARK_ELAYOUT;
   }
   {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N),
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(b_row), static_cast<cuuint64_t>(b_rows),
                                 static_cast<cuuint64_t>(G)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(sbn), static_cast<cuuint64_t>(sbg)};
-    const cuuint32_t box[3] = {128, 128, 1};
+    const cuuint32_t box[3] = {128, b_layout == 0 ? 128u : 256u, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (g_encode(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(b), dims, strides,
                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -328,7 +332,8 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
   fp.group_offs = offs;
   fp.a_scale = a_scale;
   fp.b_scale = b_scale;
-  fp.b_scale_stride = scale_stride;
+  fp.scale_stride = scale_stride;
+  fp.b_mn_major = b_layout;
   fp.G = G;
   fp.N = N;
   fp.K = K;
@@ -402,7 +407,7 @@ int ggemm_vark_grouped_fp8_fwd(const void* a, const void* b, void* c, const floa
                                void* stream) {
   return run_fwd(a, b, c, a_scale, b_scale, group_offs, G, N, K, stride_am, stride_bg, stride_bn,
                  stride_cm, stride_cn, /*m_total=*/-1, /*a_fmt=*/0, /*scale_stride=*/0,
-                 /*status=*/nullptr, /*timeout_ns=*/0, stream);
+                 /*b_layout=*/0, /*status=*/nullptr, /*timeout_ns=*/0, stream);
 }
 
 int ggemm_vark_grouped_fp8_fwd_ex(const void* a, const void* b, void* c, const float* a_scale,
@@ -410,9 +415,11 @@ int ggemm_vark_grouped_fp8_fwd_ex(const void* a, const void* b, void* c, const f
                                   int32_t N, int32_t K, int32_t stride_am, int32_t stride_bg,
                                   int32_t stride_bn, int32_t stride_cm, int32_t stride_cn,
                                   int64_t m_total, int32_t a_fmt, int32_t scale_stride,
-                                  void* status, uint64_t timeout_ns, void* stream) {
+                                  int32_t b_layout, void* status, uint64_t timeout_ns,
+                                  void* stream) {
   return run_fwd(a, b, c, a_scale, b_scale, group_offs, G, N, K, stride_am, stride_bg, stride_bn,
-                 stride_cm, stride_cn, m_total, a_fmt, scale_stride, status, timeout_ns, stream);
+                 stride_cm, stride_cn, m_total, a_fmt, scale_stride, b_layout, status,
+                 timeout_ns, stream);
 }
 
 int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out) {

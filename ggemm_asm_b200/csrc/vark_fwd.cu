@@ -3,8 +3,9 @@
 //
 // Computes, for every token t of expert g (off_g <= t < off_{g+1}),
 //     C[t, n] = sA * sB_g * sum_k A[t, k] * B[g, n, k]                 (fp32 accumulate -> bf16)
-// with A [M_total, K] (e4m3 for the forward sites, e5m2 for the data gradient) and B [G, N, K]
-// e4m3 ("trans_b": every expert's weight stored N x K). These are the four "persistent" call
+// with A [M_total, K] (e4m3 for the forward sites, e5m2 for the data gradient) and B e4m3,
+// stored [G, N, K] ("trans_b", K contiguous: the harness's layout) or [G, K, N] (N contiguous).
+// These are the four "persistent" call
 // sites of the ggemm-asm harness (bench.py:154-181: gate_up_fwd, down_fwd, down_dgrad,
 // gate_up_dgrad) with the argument layout of bench.py:312-338 (A, B, C, A_scale, B_scale,
 // group_offs, G, N, K, stride_am, stride_bg, stride_bn, stride_cm, stride_cn).
@@ -16,11 +17,15 @@
 //   * MMA-N runs along N: operand B = B[g]. The item's N columns are split N/2 per CTA. N is 256
 //     except on the last column tile, where it is the remaining columns rounded up to 16 (128 at
 //     N = 5760, 64 at N = 2880), so ragged N costs no tensor work.
-//   * Both operands are K-major (K contiguous in memory): TMA boxes of 128 K-bytes x 128 rows
-//     land in the canonical 128-byte-swizzled K-major layout; a stage is TK = 256 K values (two
-//     boxes per operand), i.e. 8 MMAs per stage, the K advance inside a box being +32 bytes on
-//     the descriptor's start address. The last stage of a K that is not a multiple of TK issues
-//     only ceil(K_rest / 32) MMAs (TMA zero-fills the part of a box beyond K).
+//   * A is K-major (K contiguous in memory): TMA boxes of 128 K-bytes x 128 rows land in the
+//     canonical 128-byte-swizzled K-major layout; a stage is TK = 256 K values (two boxes), i.e.
+//     8 MMAs per stage, the K advance inside a box being +32 bytes on the descriptor's start
+//     address. B is the same when stored [G, N, K]; stored [G, K, N] it is MN-major for the MMA:
+//     one box of 128 N-bytes x 256 K rows in the canonical 128-byte-swizzled MN-major layout,
+//     the K advance being 32 rows (4096 bytes). Then the item's N is a multiple of 32 so that
+//     each CTA's half starts on a 16-byte boundary (the TMA inner-coordinate rule). The last
+//     stage of a K that is not a multiple of TK issues only ceil(K_rest / 32) MMAs (TMA
+//     zero-fills the part of a box beyond K).
 //   * Rows of A past the expert and C rows past the expert: loads and stores go through
 //     per-expert tensor maps built on the device (base at row off_g, row extent M_g), so TMA
 //     zero-fills the A rows of a partial last token tile and clips the C store there; no
@@ -162,7 +167,8 @@ struct Walker {
     t->m0 = mt * TILE_M;
     t->rows = min(TILE_M, tokens - t->m0);
     t->n0 = nt * TILE_N;
-    t->ncols = min(TILE_N, (p->N - t->n0 + 15) & ~15);
+    const int align = p->b_mn_major ? 32 : 16;  // MN-major B: each half 16-byte aligned
+    t->ncols = min(TILE_N, (p->N - t->n0 + align - 1) & ~(align - 1));
     return true;
   }
 };
@@ -276,9 +282,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const int32_t x = kb * TK + h * KBOX;
             tma_load_2d_pair(base + OFF_A + stage * OP_STAGE + h * BOX_BYTES, gmap_a, fb, x, ya,
                              policy);
-            tma_load_3d_pair(base + OFF_B + stage * OP_STAGE + h * BOX_BYTES, &map_b, fb, x, yb,
-                             t.g, policy);
+            if (!p.b_mn_major)
+              tma_load_3d_pair(base + OFF_B + stage * OP_STAGE + h * BOX_BYTES, &map_b, fb, x, yb,
+                               t.g, policy);
           }
+          if (p.b_mn_major)  // one box: this CTA's N/2 columns x the stage's 256 K rows
+            tma_load_3d_pair(base + OFF_B + stage * OP_STAGE, &map_b, fb, yb, kb * TK, t.g,
+                             policy);
         }
         __syncwarp();
         withhold = false;
@@ -304,7 +314,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t idesc0 = idesc_f8f6f4(static_cast<uint32_t>(p.a_fmt), /*B e4m3*/ 0,
-                                           /*K-major*/ 0, 0, TILE_M, 0);
+                                           /*A K-major*/ 0,
+                                           static_cast<uint32_t>(p.b_mn_major), TILE_M, 0);
       const int nkb = (p.K + TK - 1) / TK;
       Walker w{&p, false};
       Item t;
@@ -326,7 +337,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             for (int ks = 0; ks < kmma; ++ks) {
               const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32u;
               const uint64_t adesc = smem_desc_sw128(a_stage + off, 16u, 1024u);
-              const uint64_t bdesc = smem_desc_sw128(b_stage + off, 16u, 1024u);
+              // MN-major B: K advances by 32 rows of 128 bytes; the box holds one MN atom
+              // (the N/2 <= 128 columns of this CTA), LBO = box bytes.
+              const uint64_t bdesc =
+                  p.b_mn_major ? smem_desc_sw128(b_stage + ks * 4096u, OP_STAGE, 1024u)
+                               : smem_desc_sw128(b_stage + off, 16u, 1024u);
               mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);
@@ -360,7 +375,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t epi_sh = base + OFF_EPI + (warp - EPI_WARP0) * 2 * EPI_BUF_BYTES;
     const uint32_t leader_tempty = mapa_shared(bar_tempty, 0);
-    const float a_scale = __ldg(p.a_scale);
     uint32_t acc = 0, acc_phase = 0, nstore = 0, slot = 0;
     int cur = -1;
     const CUtensorMap* gmap_c = nullptr;
@@ -372,7 +386,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         gmap_c = reinterpret_cast<const CUtensorMap*>(ring_slot(slot) + 128);
         cur = t.g;
       }
-      const float scale = a_scale * __ldg(p.b_scale + static_cast<int64_t>(t.g) * p.b_scale_stride);
+      const float scale = __ldg(p.a_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
+                          __ldg(p.b_scale + static_cast<int64_t>(t.g) * p.scale_stride);
       if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
       const int row0 = t.m0 + 128 * static_cast<int>(rank) + 32 * quarter;  // within the expert

@@ -113,14 +113,16 @@ cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
 cudaError_t tc2_set_attributes();
 
 // Fixed-K grouped GEMM (vark_fwd.cu): C[t, :] = sA * sB_g * A[t, :] . B[g]^T for the tokens t of
-// expert g; A [tokens, K] and B [G, N, K] are K-major fp8, C bf16. Tensor maps (encoded by the
-// caller): A 2D u8 {K, rows} box {128, 128}; B 3D u8 {K, N, G} box {128, 128, 1}; C 2D bf16
-// {N, rows} box {32, 32} with the 64-byte swizzle. The kernel rebuilds the A and C maps per expert.
+// expert g; A [tokens, K] is K-major fp8, B [G, N, K] (K-major) or [G, K, N] (N-major) e4m3, C
+// bf16. Tensor maps (encoded by the caller): A 2D u8 {K, rows} box {128, 128}; B 3D u8 {K, N, G}
+// box {128, 128, 1} or {N, K, G} box {128, 256, 1}; C 2D bf16 {N, rows} box {32, 32} with the
+// 64-byte swizzle. The kernel rebuilds the A and C maps per expert.
 struct FwdParams {
   const int64_t* group_offs;
-  const float* a_scale;   // one value
-  const float* b_scale;   // one value, or G values when b_scale_stride == 1
-  int32_t b_scale_stride;
+  const float* a_scale;   // one value, or G values when scale_stride == 1
+  const float* b_scale;   // likewise
+  int32_t scale_stride;
+  int32_t b_mn_major;     // 0: B [G, N, K] (K contiguous); 1: B [G, K, N] (N contiguous)
   int32_t G, N, K;
   int32_t n_tiles;        // ceil(N / 256)
   int32_t a_fmt;          // 0: e4m3, 1: e5m2 (B is e4m3)

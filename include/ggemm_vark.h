@@ -187,19 +187,24 @@ GGEMM_VARK_API int ggemm_vark_grouped_fp8_fwd(const void* a, const void* b, void
                             int32_t stride_cm, int32_t stride_cn, void* stream);
 
 /*
- * ggemm_vark_grouped_fp8_fwd_ex - the same with the A format selectable and the extensions of
- * ggemm_vark_fp8_wgrad_ex: m_total (rows allocated in A and C, or -1; offsets past it are
- * reported and their expert skipped; 0 allows NULL a, b, c), a_fmt (0: e4m3fn for the forward
- * sites, 1: e5m2 for the data-gradient sites; B stays e4m3fn), scale_stride (0: one b_scale,
- * 1: G per-expert b_scale values; a_scale is always one value), status and timeout_ns.
+ * ggemm_vark_grouped_fp8_fwd_ex - the same with the A format and B layout selectable and the
+ * extensions of ggemm_vark_fp8_wgrad_ex:
+ *  m_total       rows allocated in A and C, or -1; offsets past it are reported and their
+ *                expert skipped; 0 allows NULL a, b, c
+ *  a_fmt         0: e4m3fn (forward sites), 1: e5m2 (data-gradient sites); B stays e4m3fn
+ *  scale_stride  0: a_scale and b_scale are single values; 1: both hold G per-expert values
+ *  b_layout      0: B [G, N, K] with K contiguous ("trans_b", the harness's layout): element
+ *                (g, n, k) at b + g*stride_bg + n*stride_bn + k; 1: B [G, K, N] with N
+ *                contiguous: element (g, k, n) at b + g*stride_bg + k*stride_bn + n
+ *  status, timeout_ns  as ggemm_vark_fp8_wgrad_ex
  */
 GGEMM_VARK_API int ggemm_vark_grouped_fp8_fwd_ex(const void* a, const void* b, void* c,
                             const float* a_scale, const float* b_scale,
                             const int64_t* group_offs, int32_t G, int32_t N, int32_t K,
                             int32_t stride_am, int32_t stride_bg, int32_t stride_bn,
                             int32_t stride_cm, int32_t stride_cn, int64_t m_total,
-                            int32_t a_fmt, int32_t scale_stride, void* status,
-                            uint64_t timeout_ns, void* stream);
+                            int32_t a_fmt, int32_t scale_stride, int32_t b_layout,
+                            void* status, uint64_t timeout_ns, void* stream);
 
 /*
  * ggemm_vark_quantize_fp8 - per-expert (or per-tensor) amax scaling and FP8 quantisation of a

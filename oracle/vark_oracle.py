@@ -238,15 +238,18 @@ def quantize_fp8_ref(x: torch.Tensor, group_offs, fmt: str, per_group: bool = Tr
 
 
 def grouped_fwd_f32(a: torch.Tensor, b: torch.Tensor, a_scale, b_scale, group_offs,
-                    rows=None) -> torch.Tensor:
+                    rows=None, trans_b: bool = True) -> torch.Tensor:
     """CPU restatement of the fixed-K grouped GEMM (the harness's persistent sites, bench.py:
     154-181, checked there against Primus-Turbo's grouped_gemm_fp8_tensorwise_triton_kernel,
-    bench.py:260): per expert g, out[off_g:off_{g+1}] = sA * sB_g * a_g @ b[g]^T, fp8 decoded to
-    fp32, fp32 matmul. Returns fp32 [M, N]; `rows` (optional index tensor) restricts the output
-    to those token rows (returned in that order)."""
+    bench.py:260): per expert g, out[off_g:off_{g+1}] = sA_g * sB_g * a_g @ B_g, fp8 decoded to
+    fp32, fp32 matmul. b is [G, N, K] (trans_b: B_g = b[g]^T) or [G, K, N] (B_g = b[g]); the
+    scales hold 1 or G values. Returns fp32 [M, N]; `rows` (optional index tensor) restricts the
+    output to those token rows (returned in that order)."""
     offs = [int(v) for v in (group_offs.tolist() if hasattr(group_offs, "tolist") else group_offs)]
+    if not trans_b:
+        b = b.transpose(1, 2)
     G, N, _ = b.shape
-    sa = float(a_scale.reshape(-1)[0])
+    sa = a_scale.reshape(-1).float()
     sb = b_scale.reshape(-1).float()
     which = torch.arange(a.shape[0]) if rows is None else torch.as_tensor(rows)
     out = torch.zeros(which.numel(), N, dtype=torch.float32)
@@ -259,15 +262,16 @@ def grouped_fwd_f32(a: torch.Tensor, b: torch.Tensor, a_scale, b_scale, group_of
             continue
         ag = a[which[sel]].float()
         bg = b[g].float()
-        s = sa * float(sb[g] if sb.numel() > 1 else sb[0])
+        s = float(sa[g] if sa.numel() > 1 else sa[0]) * float(sb[g] if sb.numel() > 1 else sb[0])
         out[sel] = (ag @ bg.T) * s
     return out
 
 
-def grouped_fwd_tolerance(a, b, a_scale, b_scale, group_offs, ref: torch.Tensor, rows=None):
+def grouped_fwd_tolerance(a, b, a_scale, b_scale, group_offs, ref: torch.Tensor, rows=None,
+                          trans_b: bool = True):
     """|C - ref| bound: one bf16 ulp of |ref| plus fp32 reassociation over K terms,
-    K * 2^-24 * sA * sB * (|a| @ |b|^T) (the same form as the wgrad's)."""
+    K * 2^-24 * sA * sB * (|a| @ |B|) (the same form as the wgrad's)."""
     K = a.shape[1]
     absd = grouped_fwd_f32(_abs_fp8(a), _abs_fp8(b), a_scale.abs(), b_scale.abs(), group_offs,
-                           rows)
+                           rows, trans_b)
     return bf16_ulp(ref.abs()) + K * 2.0 ** -24 * absd

@@ -19,10 +19,13 @@ def make_fwd(lens, N, K, a_dtype=E4M3, seed=0, per_expert_scale=False):
     M, G = int(sum(lens)), len(lens)
     a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(a_dtype)
     b = torch.randn(G, N, K, generator=g).to(torch.bfloat16).to(E4M3)
-    sa = torch.tensor([0.1], dtype=torch.float32)
-    sb = (torch.rand(G, generator=g) * 0.2 + 0.05) if per_expert_scale else torch.tensor([0.1])
+    if per_expert_scale:
+        sa = torch.rand(G, generator=g) * 0.2 + 0.05
+        sb = torch.rand(G, generator=g) * 0.2 + 0.05
+    else:
+        sa, sb = torch.tensor([0.1]), torch.tensor([0.1])
     offs = torch.from_numpy(inputs.offsets_from_lens(lens))
-    return a, b, sa, sb.float(), offs
+    return a, b, sa.float(), sb.float(), offs
 
 
 # ------------------------------------------------------------------------------------------------
@@ -36,7 +39,7 @@ def test_oracle_matches_float64_restatement():
     exact = np.zeros((a.shape[0], 24))
     o = offs.tolist()
     for gi in range(4):
-        exact[o[gi]:o[gi + 1]] = ta[o[gi]:o[gi + 1]] @ tb[gi].T * 0.1 * float(sb[gi])
+        exact[o[gi]:o[gi + 1]] = ta[o[gi]:o[gi + 1]] @ tb[gi].T * float(sa[gi]) * float(sb[gi])
     tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref)
     assert (np.abs(ref.numpy() - exact) <= tol.numpy()).all()
     assert float(np.abs(exact).max()) > 0
@@ -51,11 +54,12 @@ def test_oracle_row_subset():
 
 def call_fwd(**kw):
     x = dict(a=P, b=P, c=P, sa=P, sb=P, offs=P, G=4, N=256, K=512, sam=512, sbg=256 * 512,
-             sbn=512, scm=256, scn=1, m=1024, fmt=0, ss=0, status=None)
+             sbn=512, scm=256, scn=1, m=1024, fmt=0, ss=0, lay=0, status=None)
     x.update(kw)
     return _lib.lib().ggemm_vark_grouped_fp8_fwd_ex(
         x["a"], x["b"], x["c"], x["sa"], x["sb"], x["offs"], x["G"], x["N"], x["K"], x["sam"],
-        x["sbg"], x["sbn"], x["scm"], x["scn"], x["m"], x["fmt"], x["ss"], x["status"], 0, None)
+        x["sbg"], x["sbn"], x["scm"], x["scn"], x["m"], x["fmt"], x["ss"], x["lay"], x["status"],
+        0, None)
 
 
 @pytest.mark.parametrize("kw,code", [
@@ -69,6 +73,9 @@ def call_fwd(**kw):
     (dict(status=P + 4), _lib.EINVAL_ARG),
     (dict(a=P + 8), _lib.ELAYOUT), (dict(sam=520), _lib.ELAYOUT), (dict(scn=2), _lib.ELAYOUT),
     (dict(scm=260), _lib.ELAYOUT), (dict(sbn=520, sbg=256 * 520), _lib.ELAYOUT),
+    (dict(lay=2), _lib.EINVAL_ARG), (dict(lay=1, sbn=200), _lib.EINVAL_STRIDE),
+    (dict(lay=1, sbn=256, sbg=512 * 256 - 1), _lib.EINVAL_STRIDE),
+    (dict(lay=1, sbn=264, sbg=512 * 264), _lib.ELAYOUT),
     (dict(G=0), _lib.OK), (dict(m=0, a=None, b=None, c=None), _lib.OK),
 ])
 def test_fwd_argument_checks(kw, code):
@@ -86,7 +93,7 @@ def test_torch_fwd_validates_before_launch():
     a, b, sa, sb, offs = make_fwd([4, 4], N=16, K=32)
     with pytest.raises(ValueError, match="CUDA"):
         grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="K="):
         grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs, trans_b=False)
     with pytest.raises(TypeError):
         grouped_gemm_fp8_tensorwise(a, b.view(E5M2), sa, sb, offs)
@@ -94,19 +101,21 @@ def test_torch_fwd_validates_before_launch():
         grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs[:-1])
     with pytest.raises(ValueError, match="b_scale"):
         grouped_gemm_fp8_tensorwise(a, b, sa, torch.ones(3), offs)
+    with pytest.raises(ValueError, match="b_scale"):
+        grouped_gemm_fp8_tensorwise(a, b, sa, torch.ones(2), offs)
 
 
 # ------------------------------------------------------------------------------------------------
 # GPU
 # ------------------------------------------------------------------------------------------------
-def run_gpu(a, b, sa, sb, offs, out=None, status=None):
+def run_gpu(a, b, sa, sb, offs, out=None, status=None, trans_b=True):
     return grouped_gemm_fp8_tensorwise(a.cuda(), b.cuda(), sa.cuda(), sb.cuda(), offs.cuda(),
-                                       out=out, status=status)
+                                       trans_b=trans_b, out=out, status=status)
 
 
-def check(a, b, sa, sb, offs, got, rows=None):
-    ref = vo.grouped_fwd_f32(a, b, sa, sb, offs, rows)
-    tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref, rows)
+def check(a, b, sa, sb, offs, got, rows=None, trans_b=True):
+    ref = vo.grouped_fwd_f32(a, b, sa, sb, offs, rows, trans_b)
+    tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref, rows, trans_b)
     g = got.float().cpu() if rows is None else got.float().cpu()[rows]
     err = (g - ref).abs()
     assert bool((err <= tol).all()), f"max excess {float((err - tol).max())}"
@@ -129,6 +138,24 @@ def test_fwd_matches_oracle(a_dtype, lens, N, K):
     got = run_gpu(a, b, sa, sb, offs)
     torch.cuda.synchronize()
     check(a, b, sa, sb, offs, got)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("lens,N,K", [
+    ([256], 256, 256), ([300, 0, 77, 1, 511], 320, 288), ([1000, 24], 48, 96),
+    ([129, 700], 2880, 2880), ([513], 32, 32), ([40] * 40, 272, 128), ([64, 64], 96, 544),
+])
+def test_fwd_b_k_by_n_layout(lens, N, K):
+    """trans_b=False: b [G, K, N] (N contiguous, MN-major for the MMA); the item's N rounds up
+    to 32 so each CTA's column half starts on a 16-byte boundary."""
+    a, b, sa, sb, offs = make_fwd(lens, N, K, E5M2, seed=N * 7 + K, per_expert_scale=True)
+    bt = b.transpose(1, 2).contiguous()  # [G, K, N]
+    got = run_gpu(a, bt, sa, sb, offs, trans_b=False)
+    torch.cuda.synchronize()
+    check(a, bt, sa, sb, offs, got, trans_b=False)
+    same = run_gpu(a, b, sa, sb, offs)  # the same product with b [G, N, K]
+    torch.cuda.synchronize()
+    check(a, b, sa, sb, offs, same)
 
 
 @pytest.mark.gpu

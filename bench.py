@@ -18,6 +18,11 @@ Timing: W untimed warm-up steps, then K steps between CUDA events on the launchi
 bracketed by a barrier and torch.cuda.synchronize(); the time is the max over ranks. The
 operands (1.13 GB for gate_up) are far larger than the 126 MB L2, so no L2 flush is needed.
 
+Other legs (one GPU; not the driver's line): --op quantize (the producer step: per-expert amax +
+fp8 quantisation of x and dy, GB/s), --op fwd --site <site> (the fixed-K grouped GEMM of a
+forward / data-gradient site, TFLOPS, with cuBLAS per expert beside it), --op layer (one training
+step of the FP8 MoE linear layer).
+
 --impl reference: the reference's own implementation of the path cannot run here (AMD gfx950
 code object + a Triton kernel from the absent primus_turbo package), so the reference arm
 times the CPU restatement of its algorithm (oracle/, torch fp32 dequantise + matmul per expert)
@@ -444,6 +449,29 @@ def run_fwd(args):
                       "what": "torch._scaled_mm per expert (cuBLAS), same data"}
         except Exception as exc:  # e.g. an fp8 combination cuBLAS does not take
             cublas = {"unavailable": f"{type(exc).__name__}: {str(exc)[:120]}"}
+    cpu = None
+    if not args.no_cpu_baseline:
+        # The CPU restatement (oracle, torch fp32 per expert) on a bounded sample of experts.
+        from oracle import vark_oracle as vo
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        o = offs.tolist()
+        done, secs, e = 0.0, 0.0, 0
+        sa_c, sb_c = sa.cpu(), sb.cpu()
+        for e in range(G):
+            lo, hi = o[e], o[e + 1]
+            if hi == lo:
+                continue
+            ac = a[lo:hi].cpu()
+            bc = b[e:e + 1].cpu()
+            t_s = time.perf_counter()
+            vo.grouped_fwd_f32(ac, bc, sa_c, sb_c, [0, hi - lo])
+            secs += time.perf_counter() - t_s
+            done += 2.0 * (hi - lo) * N * K
+            if secs > args.cpu_seconds:
+                break
+        cpu = {"value": done / secs / 1e12, "unit": "TFLOPS", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"experts 0..{e} by the torch CPU oracle; {secs:.1f} s"}
     fp8_peak, _hbm, peak_src = measured_peaks()
     line = {
         "metric": f"{args.site} fixed-K grouped FP8 GEMM TFLOPS", "value": value, "unit": "TFLOPS",
@@ -458,7 +486,7 @@ def run_fwd(args):
                      "frac_of_nominal_4500": value / FP8_NOMINAL_TFLOPS,
                      "kernel": "vark_fwd2_kernel", "traffic": profile_traffic(args.site)},
         "cublas_per_expert": cublas, "clocks": clocks, "gpu_launches": args.steps, "e2e": None,
-        "cpu_baseline": None,
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
 

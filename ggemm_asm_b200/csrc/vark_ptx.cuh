@@ -1,7 +1,7 @@
 // vark_ptx.cuh - thin inline-PTX wrappers for the sm_100a variable-K wgrad kernel.
 //
 // Each wrapper is one PTX instruction (or a tiny fixed sequence) from the PTX ISA for
-// sm_100a: mbarrier.*, cp.async.bulk.tensor.* (TMA, no cluster multicast anywhere),
+// sm_100a: mbarrier.*, cp.async.bulk.tensor.* (TMA, plain per-CTA forms only),
 // tcgen05.{alloc,dealloc,mma,commit,ld,wait,fence}. Nothing here is specific to the problem;
 // the kernel in vark_tc.cu composes them.
 #pragma once
@@ -64,7 +64,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor) - plain loads/stores, never .multicast::cluster
+// TMA (cp.async.bulk.tensor) - plain loads/stores: every load fills one CTA's shared memory
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -251,7 +251,8 @@ __device__ __forceinline__ void tmem_regs_fence(uint32_t (&r)[N]) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Clusters of two CTAs (cta_group::2). No TMA multicast is used anywhere in this library.
+// Clusters of two CTAs (cta_group::2). Every TMA load in this library fills one CTA's own
+// shared memory (the .cta_group::2 form only signals the pair leader's barrier).
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -689,7 +689,7 @@ def main():
         h2d = (sum(t.numel() * t.element_size() for t in (h_lhs, h_rhs, h_ls, h_rs))
                + h_offs_np.nbytes)
         d2h = h_out.numel() * h_out.element_size()
-        pipe = HostWgrad(p.lhs.shape[0], p.G, p.OUT_M, p.OUT_N, device=device, chunks=8)
+        pipe = HostWgrad(p.lhs.shape[0], p.G, p.OUT_M, p.OUT_N, device=device, chunks=16)
 
         def e2e_step():
             pipe(h_lhs, h_rhs, h_ls, h_rs, h_offs_np, h_out)
@@ -736,7 +736,7 @@ def main():
         e2e = {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                "steps": e2e_steps,
-               "api": "ggemm_asm_b200.host.HostWgrad (8 expert chunks, copies overlapped)",
+               "api": "ggemm_asm_b200.host.HostWgrad (16 expert chunks, copies overlapped)",
                "serial": {"value": flops_total / (serial_ms * 1e-3) / 1e12,
                           "ms_per_step": serial_ms,
                           "api": "copy in, one grouped_gemm_fp8_tensorwise_variable_k, copy out"}}

@@ -173,6 +173,17 @@ struct Walker {
   }
 };
 
+// Shared-memory descriptor offsets of MMA ks (K step of 32) inside a stage, in descriptor units
+// (16 bytes): A and K-major B advance 32 bytes inside a 128-byte box and then jump to the next
+// box; MN-major B advances 32 rows of 128 bytes.
+__device__ __forceinline__ uint64_t kmajor_step(int ks) {
+  return static_cast<uint64_t>(((ks >> 2) * BOX_BYTES + (ks & 3) * 32u) >> 4);
+}
+__device__ __forceinline__ uint64_t mnmajor_step(int ks) {
+  return static_cast<uint64_t>((ks * 4096u) >> 4);
+}
+
+template <bool BMN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     vark_fwd2_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
@@ -282,11 +293,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const int32_t x = kb * TK + h * KBOX;
             tma_load_2d_pair(base + OFF_A + stage * OP_STAGE + h * BOX_BYTES, gmap_a, fb, x, ya,
                              policy);
-            if (!p.b_mn_major)
+            if (!BMN)
               tma_load_3d_pair(base + OFF_B + stage * OP_STAGE + h * BOX_BYTES, &map_b, fb, x, yb,
                                t.g, policy);
           }
-          if (p.b_mn_major)  // one box: this CTA's N/2 columns x the stage's 256 K rows
+          if (BMN)  // one box: this CTA's N/2 columns x the stage's 256 K rows
             tma_load_3d_pair(base + OFF_B + stage * OP_STAGE, &map_b, fb, yb, kb * TK, t.g,
                              policy);
         }
@@ -314,8 +325,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t idesc0 = idesc_f8f6f4(static_cast<uint32_t>(p.a_fmt), /*B e4m3*/ 0,
-                                           /*A K-major*/ 0,
-                                           static_cast<uint32_t>(p.b_mn_major), TILE_M, 0);
+                                           /*A K-major*/ 0, BMN ? 1u : 0u, TILE_M, 0);
       const int nkb = (p.K + TK - 1) / TK;
       Walker w{&p, false};
       Item t;
@@ -331,18 +341,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after_sync();
           const int kmma = min(TK / 32, (p.K - kb * TK + 31) / 32);
-          const uint32_t a_stage = base + OFF_A + stage * OP_STAGE;
-          const uint32_t b_stage = base + OFF_B + stage * OP_STAGE;
           if (lane == 0) {
-            for (int ks = 0; ks < kmma; ++ks) {
-              const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32u;
-              const uint64_t adesc = smem_desc_sw128(a_stage + off, 16u, 1024u);
-              // MN-major B: K advances by 32 rows of 128 bytes; the box holds one MN atom
-              // (the N/2 <= 128 columns of this CTA), LBO = box bytes.
-              const uint64_t bdesc =
-                  p.b_mn_major ? smem_desc_sw128(b_stage + ks * 4096u, OP_STAGE, 1024u)
-                               : smem_desc_sw128(b_stage + off, 16u, 1024u);
-              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+            // Stage descriptors; each MMA adds a constant offset. MN-major B: the box holds one
+            // MN atom (the N/2 <= 128 columns of this CTA), LBO = box bytes.
+            const uint64_t a0 = smem_desc_sw128(base + OFF_A + stage * OP_STAGE, 16u, 1024u);
+            const uint64_t b0 = BMN ? smem_desc_sw128(base + OFF_B + stage * OP_STAGE, OP_STAGE,
+                                                      1024u)
+                                    : smem_desc_sw128(base + OFF_B + stage * OP_STAGE, 16u, 1024u);
+            if (kmma == TK / 32) {
+#pragma unroll
+              for (int ks = 0; ks < TK / 32; ++ks)
+                mma_f8f6f4_pair(d_tmem, a0 + kmajor_step(ks),
+                                b0 + (BMN ? mnmajor_step(ks) : kmajor_step(ks)), idesc,
+                                (kb > 0 || ks > 0) ? 1u : 0u);
+            } else {  // the K tail
+              for (int ks = 0; ks < kmma; ++ks)
+                mma_f8f6f4_pair(d_tmem, a0 + kmajor_step(ks),
+                                b0 + (BMN ? mnmajor_step(ks) : kmajor_step(ks)), idesc,
+                                (kb > 0 || ks > 0) ? 1u : 0u);
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);
           }
@@ -475,12 +491,19 @@ size_t fwd2_smem_bytes() { return SMEM_ALLOC; }
 cudaError_t fwd2_launch(const CUtensorMap& map_a, const CUtensorMap& map_b,
                         const CUtensorMap& map_c, const FwdParams& p, int grid,
                         cudaStream_t stream) {
-  vark_fwd2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_a, map_b, map_c, p);
+  if (p.b_mn_major)
+    vark_fwd2_kernel<true><<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_a, map_b, map_c, p);
+  else
+    vark_fwd2_kernel<false><<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_a, map_b, map_c, p);
   return cudaGetLastError();
 }
 
 cudaError_t fwd2_set_attributes() {
-  return cudaFuncSetAttribute(vark_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(vark_fwd2_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(SMEM_ALLOC));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(vark_fwd2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(SMEM_ALLOC));
 }
 

@@ -14,6 +14,12 @@
 //     tile, where it is the remaining rows rounded up to 32 (64 for OUT_M = 2880 = 11x256 + 64),
 //     so ragged OUT_M costs no tensor work. Along OUT_N the waste is at most one 128-column half
 //     (2.2% at 5760 = 45 x 128).
+// The last column tile is different when OUT_N is not a multiple of 256 (5760 = 22.5 x 256,
+// 2880 = 11.25 x 256): most of its 256 MMA-M rows would be padding. Those items are computed
+// transposed: MMA-M = 256 runs along OUT_M (A = LHS e4m3, 128 C rows per CTA, one per TMEM lane)
+// and MMA-N along the remaining columns rounded up to 32 (B = RHS e5m2, half per CTA), with a
+// non-transposed epilogue. Same item count and order; the padding shrinks from 256 - E columns
+// per row tile to at most 31 (and the rows of the last row tile, as for any 256-row M tile).
 // Both operands stay in their token-major layout, which for the MMA is MN-major: a TMA box of
 // 128 contiguous features x TK tokens lands with the 128-byte swizzle of the canonical MN-major
 // layout. Per CTA and TK tokens that is 2 x 128 x TK bytes for 128 x 256 x TK MACs. Boxes that
@@ -90,9 +96,11 @@ constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0, "alignment");
 
-// Instruction descriptor without N: the item's N is or-ed in at run time.
+// Instruction descriptors without N: the item's N is or-ed in at run time.
 constexpr uint32_t IDESC_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
                                              /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
+constexpr uint32_t IDESC_EDGE_NO_N = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
+                                                  /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
 
 struct Ctl {
   volatile int* abort;
@@ -132,6 +140,8 @@ struct Item {
   int nrows;       // MMA N: C rows of the item, a multiple of 32 (<= 256)
   int tokens;      // K_g (0 for empty or invalid groups)
   int64_t end;     // off_{g+1}
+  bool edge;       // last, partial column tile: computed transposed (see the file comment)
+  int ecols;       // edge item's MMA N: its C columns rounded up to 32
 };
 
 __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool report) {
@@ -142,6 +152,8 @@ __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool re
   t.n0 = (r % p.col_tiles) * ITEM_COLS;
   t.m0 = (r / p.col_tiles) * ITEM_ROWS;
   t.nrows = min(ITEM_ROWS, (p.OUT_M - t.m0 + 31) & ~31);
+  t.edge = t.n0 + ITEM_COLS > p.OUT_N;
+  t.ecols = (p.OUT_N - t.n0 + 31) & ~31;
   const int64_t lo = __ldg(p.group_offs + t.g);
   const int64_t hi = __ldg(p.group_offs + t.g + 1);
   if (lo < 0 || hi < lo || hi > p.token_limit) {
@@ -258,10 +270,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       const int nkb = (t.tokens + TK - 1) / TK;
       const int32_t y0 = t.tokens - TK * nkb;  // <= 0: rows before the group read as zeros
-      // A: this CTA's 128 C columns; B: this CTA's half of the item's rows (N/2 is a multiple
-      // of 16, so the TMA x coordinate stays 16-byte aligned).
-      const int32_t xr = t.n0 + PAIR_HALF * static_cast<int32_t>(rank);
-      const int32_t xl = t.m0 + (t.nrows >> 1) * static_cast<int32_t>(rank);
+      // A: this CTA's 128 C columns (RHS); B: this CTA's half of the item's rows (LHS). Edge
+      // items swap them: A = 128 C rows (LHS), B = half of the edge columns (RHS). Every N/2 is
+      // a multiple of 16, so the TMA x coordinates stay 16-byte aligned.
+      const int32_t r = static_cast<int32_t>(rank);
+      const int32_t xa = t.edge ? t.m0 + PAIR_HALF * r : t.n0 + PAIR_HALF * r;
+      const int32_t xb = t.edge ? t.n0 + (t.ecols >> 1) * r : t.m0 + (t.nrows >> 1) * r;
+      const CUtensorMap* const map_a = t.edge ? gmap_lhs : gmap_rhs;
+      const CUtensorMap* const map_b = t.edge ? gmap_rhs : gmap_lhs;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
           ok = false;
@@ -271,8 +287,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
           mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
           const int32_t y = y0 + TK * kb;
-          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, gmap_rhs, fb, xr, y, policy);
-          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, gmap_lhs, fb, xl, y, policy);
+          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, map_a, fb, xa, y, policy);
+          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, map_b, fb, xb, y, policy);
         }
         __syncwarp();
         withhold = false;
@@ -312,7 +328,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
-        const uint32_t idesc = IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
+        const uint32_t idesc = t.edge ? IDESC_EDGE_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
+                                      : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
             ok = false;
@@ -375,12 +392,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     for (int item = cluster; item < num_items; item += nclusters) {
       const Item t = nxt;
       if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, reporter);
-      const int xcol = t.n0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;  // first C col
-      const bool cols_live = xcol < p.OUT_N;
-      const int rows_here = min(t.nrows, p.OUT_M - t.m0);
-      const int nchunks = (rows_here + EPI_ROWS - 1) / EPI_ROWS;
+      // This warp's 32 TMEM lanes are 32 C columns starting at xcol (normal items) or 32 C rows
+      // starting at row0 (edge items); TMEM column chunk c is 32 C rows (normal) or 32 C
+      // columns (edge) of those.
+      const int xcol = t.n0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;
+      const int row0 = t.m0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;
+      const bool live = t.edge ? row0 < p.OUT_M : xcol < p.OUT_N;
+      const int span = t.edge ? min(t.ecols, p.OUT_N - t.n0) : min(t.nrows, p.OUT_M - t.m0);
+      const int nchunks = (span + 31) / 32;
       if (t.tokens == 0) {
-        if (cols_live) {
+        if (live) {
           const uint32_t buf = next_buf();
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -391,8 +412,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            for (int c = half; c < nchunks; c += EPI_SPLIT)
-              tma_store_3d(&map_c, buf, xcol, t.m0 + c * EPI_ROWS, t.g);
+            for (int c = half; c < nchunks; c += EPI_SPLIT) {
+              if (t.edge)
+                tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, row0, t.g);
+              else
+                tma_store_3d(&map_c, buf, xcol, t.m0 + c * EPI_ROWS, t.g);
+            }
             bulk_commit_group();
           }
           ++nstore;
@@ -403,7 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                           __ldg(p.rhs_scale + static_cast<int64_t>(t.g) * p.scale_stride);
       if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
-      if (cols_live) {
+      if (live) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
         // This lane holds C column xcol + lane for the 32 C rows of TMEM columns [32c, 32c+32).
         // The 32x32 box is stored row-major (64-byte rows) with the 64-byte swizzle the C tensor
@@ -414,6 +439,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const uint32_t odd = static_cast<uint32_t>(lane) & 1u;
         auto emit = [&](uint32_t (&r)[32], int c) {
           const uint32_t buf = next_buf();
+          if (t.edge) {
+            // Edge item: this lane holds 32 consecutive C columns of C row row0 + lane: one
+            // 64-byte row of the box, four 16-byte pieces at the 64-byte swizzle's positions.
+            const uint32_t row = static_cast<uint32_t>(lane);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t v[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 b2 =
+                    __floats2bfloat162_rn(__uint_as_float(r[8 * q4 + 2 * e]) * scale,
+                                          __uint_as_float(r[8 * q4 + 2 * e + 1]) * scale);
+                v[e] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              const uint32_t addr =
+                  buf + row * 64u + ((static_cast<uint32_t>(q4) ^ ((row >> 1) & 3u)) << 4);
+              asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]),
+                           "r"(v[1]), "r"(v[2]), "r"(v[3])
+                           : "memory");
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, row0, t.g);
+              bulk_commit_group();
+            }
+            ++nstore;
+            return;
+          }
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             const float v0 = __uint_as_float(r[j]) * scale;

@@ -74,7 +74,9 @@ def test_ragged_groups(lens, path):
 
 
 @pytest.mark.parametrize("shape", [(240, 128), (480, 256), (16, 16), (2880, 128), (64, 5760),
-                                   (496, 400), (256, 256), (272, 272), (128, 640)])
+                                   (496, 400), (256, 256), (272, 272), (128, 640),
+                                   # last column tile widths 64, 96, 224, 32 (transposed items)
+                                   (2880, 2880), (112, 96), (304, 480), (48, 224), (512, 32)])
 @pytest.mark.parametrize("path", TC_PATHS)
 def test_tile_edges(shape, path):
     OUT_M, OUT_N = shape

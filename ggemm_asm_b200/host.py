@@ -24,7 +24,9 @@ class HostWgrad:
     call(lhs_h, rhs_h, lhs_scale, rhs_scale, group_offs_h, out_h): lhs_h [M, OUT_M] e4m3 and
     rhs_h [M, OUT_N] e5m2 in pinned host memory, scales fp32 (1 or G elements; host or device),
     group_offs_h host int64 [G+1], out_h pinned host bf16 [G, OUT_M, OUT_N]. Returns out_h once
-    its contents are on the host (the call synchronises with its last copy).
+    its contents are on the host (the call synchronises with its last copy). One instance owns
+    its device buffers and streams: calls on the same instance must not overlap (use one
+    instance per thread).
     """
 
     def __init__(self, max_tokens: int, G: int, OUT_M: int, OUT_N: int, device="cuda",

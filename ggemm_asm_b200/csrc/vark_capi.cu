@@ -23,10 +23,7 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 constexpr int64_t kTokenCoordLimit = INT32_MAX;        // TMA coordinates are int32
-// SM identifiers (%smid) the tensor-map ring covers; %smid is below the SM count on B200 but
-// the PTX ISA does not promise contiguity, so the ring is sized generously (512 KiB).
-constexpr int kTmapSmIds = 256;
-constexpr size_t kStatusBytes = 4096;  // status words, then the 128-byte aligned ring
+constexpr size_t kStatusBytes = 4096;  // status words
 
 thread_local int t_last_cuda_error = 0;
 
@@ -35,7 +32,6 @@ struct DeviceState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
   uint32_t* status = nullptr;    // status block owned by the library
-  uint8_t* tmap_ring = nullptr;  // per-SM ring of device-built tensor maps
 };
 
 std::mutex g_mutex;
@@ -70,16 +66,15 @@ int get_device(DeviceState** out, int* dev_out) {
     if ((e = vark::tc_set_attributes()) != cudaSuccess) return fail_cuda(e);
     if ((e = vark::tc2_set_attributes()) != cudaSuccess) return fail_cuda(e);
     if ((e = vark::fwd2_set_attributes()) != cudaSuccess) return fail_cuda(e);
-    // One allocation per device, kept until exit: the status block and the tensor-map ring.
+    // One allocation per device, kept until exit: the status block.
     void* blk = nullptr;
-    const size_t bytes = kStatusBytes + vark::tc_tmap_ring_bytes(kTmapSmIds);
+    const size_t bytes = kStatusBytes;
     if ((e = cudaMalloc(&blk, bytes)) != cudaSuccess) return fail_cuda(e);
     if ((e = cudaMemset(blk, 0, bytes)) != cudaSuccess) {
       cudaFree(blk);
       return fail_cuda(e);
     }
     s.status = static_cast<uint32_t*>(blk);
-    s.tmap_ring = static_cast<uint8_t*>(blk) + kStatusBytes;
     if (g_encode == nullptr) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -100,11 +95,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool tc_layout_ok(const void* lhs, const void* rhs, void* c, int32_t OUT_M, int32_t OUT_N,
                   int32_t slm, int32_t srm, int32_t scg, int32_t scm, int32_t scn) {
   (void)OUT_M;
-  (void)OUT_N;
   if (!aligned16(lhs) || !aligned16(rhs) || !aligned16(c)) return false;
   if (slm % 16 != 0 || srm % 16 != 0) return false;              // fp8 row pitch, bytes
   if (scn != 1) return false;                                     // C rows contiguous
   if ((2ll * scm) % 16 != 0 || (2ll * scg) % 16 != 0) return false;  // bf16 pitches
+  // A TMA store writes a C row up to the next 16-byte boundary: with OUT_N % 8 != 0 it would
+  // overwrite up to 7 of the caller's columns past OUT_N.
+  if (OUT_N % 8 != 0) return false;
   return true;
 }
 
@@ -241,12 +238,6 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.token_limit = token_limit;
   tp.status = st;
   tp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
-  tp.lhs = static_cast<const uint8_t*>(lhs);
-  tp.rhs = static_cast<const uint8_t*>(rhs);
-  tp.stride_lhs = slm;
-  tp.stride_rhs = srm;
-  tp.tmap_ring = dev->tmap_ring;
-  tp.num_sms = kTmapSmIds;
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = scg;
   tp.stride_cm = scm;
@@ -291,7 +282,8 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
   const int64_t token_limit =
       m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
 
-  // A [rows, K] u8 and C [rows, N] bf16: the kernel replaces base and row extent per expert.
+  // A [rows, K] u8 and C [rows, N] bf16 over all M_total rows: the kernel addresses an expert's
+  // rows by coordinate (off_g + row) and writes each expert's ragged last rows without TMA.
   CUtensorMap map_a, map_b, map_c;
   const uint64_t rows = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
   {
@@ -342,12 +334,8 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
   fp.token_limit = token_limit;
   fp.status = status != nullptr ? static_cast<uint32_t*>(status) : dev->status;
   fp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
-  fp.a = static_cast<const uint8_t*>(a);
-  fp.stride_am = sam;
   fp.c = static_cast<uint16_t*>(c);
   fp.stride_cm = scm;
-  fp.tmap_ring = dev->tmap_ring;
-  fp.num_sms = kTmapSmIds;
   // The item count depends on the group sizes, which stay on the device: one cluster per pair
   // of SMs, each walking the items round-robin (clusters without items exit at once).
   const cudaError_t e = vark::fwd2_launch(map_a, map_b, map_c, fp, 2 * (dev->sm_count / 2),

@@ -26,21 +26,26 @@
 //     each CTA's half starts on a 16-byte boundary (the TMA inner-coordinate rule). The last
 //     stage of a K that is not a multiple of TK issues only ceil(K_rest / 32) MMAs (TMA
 //     zero-fills the part of a box beyond K).
-//   * Rows of A past the expert and C rows past the expert: loads and stores go through
-//     per-expert tensor maps built on the device (base at row off_g, row extent M_g), so TMA
-//     zero-fills the A rows of a partial last token tile and clips the C store there; no
-//     expert's output touches another's rows.
+//   * Rows past the expert: A and C go through the launch's own tensor maps over all M_total
+//     rows (no map is built on the device). The A rows of a partial last token tile are the
+//     next expert's tokens (or zero fill past M_total); their accumulator rows are computed and
+//     never stored. C is stored 32 rows at a time: a warp whose 32 rows all belong to the
+//     expert stores them with TMA; the warp holding the expert's ragged last rows writes only
+//     those rows with plain stores, clipped to N, so no expert's output touches another's rows.
+//     A TMA store writes a row up to the next 16-byte boundary, so when N is not a multiple of
+//     8 the 32-column chunk that crosses N is written with plain stores as well: nothing past
+//     column N - 1 is touched.
 //
 // Warp roles (6 warps, one CTA per SM, 74 pairs on 148 SMs, persistent over a static round-robin
 // of work items by cluster; items ordered expert, token tile, column tile):
-//   warp 0      TMA producer (both CTAs): builds the expert's A and C maps on a change of expert
-//               and publishes them to this SM's slice of the map ring; ring of ST stages
-//               {A 128 x 256, B N/2 x 256}, completion counted on the pair leader's barrier
+//   warp 0      TMA producer (both CTAs): ring of ST stages {A 128 x 256, B N/2 x 256},
+//               completion counted on the pair leader's barrier
 //   warp 1      TMEM owner (both CTAs; all 512 columns = two 128-lane x 256-column fp32
 //               accumulators); in the leader also the MMA issuer
 //   warps 2..5  epilogue (both CTAs): tcgen05.ld 32 TMEM columns of this warp's 32 rows ->
 //               * (sA * sB_g) -> bf16 (RNE) -> one 64-byte row per lane of a 64B-swizzled
-//               32 x 32 smem box -> TMA store through the expert's C map
+//               32 x 32 smem box -> TMA store (or, for the expert's ragged last rows, plain
+//               16-byte stores straight from the registers)
 //
 // Every mbarrier wait is bounded (FwdParams::timeout_ns). On expiry the CTA flags
 // GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs, every role leaves its loop,
@@ -75,14 +80,13 @@ constexpr uint32_t EPI_BUF_BYTES = EPI_COLS * EPI_ROWS * 2;
 constexpr uint32_t OFF_A = 0;
 constexpr uint32_t OFF_B = OFF_A + ST * OP_STAGE;
 constexpr uint32_t OFF_EPI = OFF_B + ST * OP_STAGE;
-constexpr uint32_t OFF_TMAP = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
+constexpr uint32_t OFF_BARS = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
 constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
 constexpr uint32_t SMEM_USED = OFF_MISC + 16;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
-static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0 && OP_STAGE % 1024 == 0, "alignment");
+static_assert(OFF_EPI % 1024 == 0 && OP_STAGE % 1024 == 0, "alignment");
 
 struct Ctl {
   volatile int* abort;
@@ -233,10 +237,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 p.status, p.timeout_ns};
   const int64_t cluster = cluster_id_x();
   const int64_t nclusters = num_clusters_x();
-  const uint32_t smid = sm_id();
-  auto ring_slot = [&](uint32_t slot) {
-    return p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
-  };
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) =======================================
@@ -244,41 +244,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     bool withhold =
         p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
                                    GGEMM_VARK_TEST_STALL_MAGIC;
-    const uint32_t smem_maps = base + OFF_TMAP;
-    uint32_t stage = 0, phase = 0, slot = 0;
-    int cur = -1;
-    const CUtensorMap* gmap_a = nullptr;
-    bool ok = smid < static_cast<uint32_t>(p.num_sms);
-    if (!ok && lane == 0) report_timeout(ctl, 0x500u);
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
     Walker w{&p, false};
     Item t;
     const int nkb = (p.K + TK - 1) / TK;
     for (int64_t item = cluster; ok && w.seek(item, &t); item += nclusters) {
-      if (t.g != cur) {
-        // This expert's A map (rows off_g.., extent M_g) and C map, published to the ring.
-        slot = (slot + 1) % TMAP_SLOTS;
-        uint8_t* const pair = ring_slot(slot);
-        if (lane < 16) {
-          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_a : &map_c);
-          reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
-        }
-        __syncwarp();
-        if (lane == 0) {
-          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.a + t.lo * p.stride_am));
-          tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
-          tmap_set_address(smem_maps + 128,
-                           reinterpret_cast<uint64_t>(p.c + t.lo * p.stride_cm));
-          tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
-        }
-        __syncwarp();
-        tmap_publish(pair, smem_maps);
-        tmap_publish(pair + 128, smem_maps + 128);
-        gmap_a = reinterpret_cast<const CUtensorMap*>(pair);
-        if (lane == 0) tmap_acquire(gmap_a);
-        __syncwarp();
-        cur = t.g;
-      }
-      const int32_t ya = t.m0 + 128 * static_cast<int32_t>(rank);
+      // Token rows of this CTA's half of the tile, as rows of the whole A (off_g + m0 + 128r;
+      // below the token coordinate limit, so it fits the TMA's int32 coordinate).
+      const int32_t ya = static_cast<int32_t>(t.lo) + t.m0 + 128 * static_cast<int32_t>(rank);
       const int32_t yb = t.n0 + (t.ncols >> 1) * static_cast<int32_t>(rank);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
@@ -291,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int32_t x = kb * TK + h * KBOX;
-            tma_load_2d_pair(base + OFF_A + stage * OP_STAGE + h * BOX_BYTES, gmap_a, fb, x, ya,
+            tma_load_2d_pair(base + OFF_A + stage * OP_STAGE + h * BOX_BYTES, &map_a, fb, x, ya,
                              policy);
             if (!BMN)
               tma_load_3d_pair(base + OFF_B + stage * OP_STAGE + h * BOX_BYTES, &map_b, fb, x, yb,
@@ -391,31 +365,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t epi_sh = base + OFF_EPI + (warp - EPI_WARP0) * 2 * EPI_BUF_BYTES;
     const uint32_t leader_tempty = mapa_shared(bar_tempty, 0);
-    uint32_t acc = 0, acc_phase = 0, nstore = 0, slot = 0;
-    int cur = -1;
-    const CUtensorMap* gmap_c = nullptr;
+    uint32_t acc = 0, acc_phase = 0, nstore = 0;
     Walker w{&p, leader && warp == EPI_WARP0 && lane == 0};
     Item t;
     for (int64_t item = cluster; w.seek(item, &t); item += nclusters) {
-      if (t.g != cur) {  // the producer published this expert's maps in the same ring order
-        slot = (slot + 1) % TMAP_SLOTS;
-        gmap_c = reinterpret_cast<const CUtensorMap*>(ring_slot(slot) + 128);
-        cur = t.g;
-      }
       const float scale = __ldg(p.a_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
                           __ldg(p.b_scale + static_cast<int64_t>(t.g) * p.scale_stride);
       if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
       const int row0 = t.m0 + 128 * static_cast<int>(rank) + 32 * quarter;  // within the expert
       if (row0 < t.tokens) {
-        if (lane == 0) tmap_acquire(gmap_c);
-        __syncwarp();
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
         // 32-column chunks up to the last real column (the store clips columns >= N).
         const int nchunks = (min(t.ncols, p.N - t.n0) + EPI_COLS - 1) / EPI_COLS;
-        // Lane = token row; a chunk is 32 consecutive columns = one 64-byte row of the box,
-        // written as four 16-byte pieces at the 64-byte swizzle's positions (piece ^ (row>>1)&3).
+        // This warp's rows of the expert: all 32, or the expert's ragged last rows.
+        const int live_rows = min(EPI_ROWS, t.tokens - row0);
+        const int32_t crow0 = static_cast<int32_t>(t.lo) + row0;  // as a row of C
+        // Lane = token row; a chunk is 32 consecutive columns. Eight of them -> four bf16 pairs.
+        auto pack = [&](const uint32_t (&r)[32], int q, uint32_t (&v)[4]) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 b2 =
+                __floats2bfloat162_rn(__uint_as_float(r[8 * q + 2 * e]) * scale,
+                                      __uint_as_float(r[8 * q + 2 * e + 1]) * scale);
+            v[e] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+        };
         auto emit = [&](uint32_t (&r)[32], int c) {
+          const int col0 = t.n0 + c * EPI_COLS;
+          // A TMA store writes each row up to the next 16-byte boundary, so the chunk that
+          // crosses an N that is not a multiple of 8 goes the plain way too.
+          if (live_rows < EPI_ROWS || ((p.N & 7) != 0 && col0 + EPI_COLS > p.N)) {
+            // The expert's last rows (or the last chunk of a ragged N): each live lane writes
+            // its row's 32 columns (clipped to N) as 16-byte pieces; C rows are 16-byte aligned
+            // (the row pitch is a multiple of 8 elements) and col0 is a multiple of 32.
+            if (lane < live_rows) {
+              const int ncv = min(EPI_COLS, p.N - col0);
+              uint16_t* const dst = p.c + static_cast<int64_t>(crow0 + lane) * p.stride_cm + col0;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t v[4];
+                pack(r, q, v);
+                if (8 * q + 8 <= ncv) {
+                  *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(v[0], v[1], v[2], v[3]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    if (8 * q + e < ncv)
+                      dst[8 * q + e] = static_cast<uint16_t>(v[e >> 1] >> (16 * (e & 1)));
+                }
+              }
+            }
+            return;
+          }
+          // Full 32 rows: one 64-byte row per lane of a 64B-swizzled box, written as four
+          // 16-byte pieces at the swizzle's positions (piece ^ (row>>1)&3), then one TMA store.
           const uint32_t buf = epi_sh + (nstore & 1u) * EPI_BUF_BYTES;
           if (lane == 0) bulk_wait_group_read<1>();
           __syncwarp();
@@ -423,13 +427,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 b2 =
-                  __floats2bfloat162_rn(__uint_as_float(r[8 * q + 2 * e]) * scale,
-                                        __uint_as_float(r[8 * q + 2 * e + 1]) * scale);
-              v[e] = *reinterpret_cast<const uint32_t*>(&b2);
-            }
+            pack(r, q, v);
             const uint32_t addr = buf + row * 64u + ((static_cast<uint32_t>(q) ^ ((row >> 1) & 3u)) << 4);
             asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]),
                          "r"(v[1]), "r"(v[2]), "r"(v[3])
@@ -438,7 +436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(gmap_c, buf, t.n0 + c * EPI_COLS, row0);
+            tma_store_2d(&map_c, buf, col0, crow0);
             bulk_commit_group();
           }
           ++nstore;

@@ -39,10 +39,6 @@ constexpr int PAIR_ROWS_MAX = 256;          // C rows per work item (the last on
 constexpr int PAIR_STAGES = VARK_PAIR_STAGES;
 constexpr int PAIR_TOKENS = VARK_PAIR_TK;   // tokens per pipeline stage of the pair kernel
 
-// Per-SM ring of device-built tensor-map pairs (RHS, LHS) for the group being loaded.
-constexpr int TMAP_SLOTS = 8;
-constexpr int TMAP_PAIR_BYTES = 256;
-
 // Per-warp C staging box of the epilogue (columns x rows), written with one TMA store.
 constexpr int EPI_BOX_COLS = 32;
 constexpr int EPI_BOX_ROWS = 16;
@@ -60,21 +56,10 @@ struct TcParams {
   int64_t token_limit;   // group offsets above this are invalid
   uint32_t* status;      // device status block (bit flags in word 0)
   uint64_t timeout_ns;   // limit on one pipeline wait
-  const uint8_t* lhs;    // operand bases (per-group tensor maps point inside them)
-  const uint8_t* rhs;
-  int64_t stride_lhs;    // row pitches in bytes
-  int64_t stride_rhs;
-  uint8_t* tmap_ring;    // num_SMs * TMAP_SLOTS * TMAP_PAIR_BYTES bytes, 128-byte aligned
-  int32_t num_sms;       // SM count the ring was sized for
   uint16_t* c;           // C (bf16 bits) and its element strides, for direct stores
   int64_t stride_cg;
   int64_t stride_cm;
 };
-
-// Bytes of tensor-map ring the tcgen05 kernel needs on a device with `num_sms` SMs.
-inline size_t tc_tmap_ring_bytes(int num_sms) {
-  return static_cast<size_t>(num_sms) * TMAP_SLOTS * TMAP_PAIR_BYTES;
-}
 
 // Dynamic shared memory the tcgen05 kernel needs (bytes, including alignment slack).
 size_t tc_smem_bytes();
@@ -129,12 +114,8 @@ struct FwdParams {
   int64_t token_limit;    // group offsets above this are invalid
   uint32_t* status;
   uint64_t timeout_ns;
-  const uint8_t* a;       // A base; row pitch in bytes
-  int64_t stride_am;
-  uint16_t* c;            // C base (bf16 bits); row pitch in elements
+  uint16_t* c;            // C base (bf16 bits); row pitch in elements (a multiple of 8)
   int64_t stride_cm;
-  uint8_t* tmap_ring;     // as TcParams::tmap_ring
-  int32_t num_sms;
 };
 size_t fwd2_smem_bytes();
 cudaError_t fwd2_launch(const CUtensorMap& map_a, const CUtensorMap& map_b,

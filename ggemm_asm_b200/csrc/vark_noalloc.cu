@@ -4,16 +4,15 @@
 // memory pool or arena owned by a framework (every byte must come from the arena), allocators
 // with strict accounting, processes that fixed their device footprint up front, and paths that
 // must not hit the device-wide synchronisation cudaMalloc/cudaFree can imply. The regular entry
-// points make one cudaMalloc per device on first use (status words plus the ring of tensor maps
-// the kernel builds). This entry point runs the same CTA-pair tensor-core kernel with that
-// scratch taken from a fixed, file-scope device array instead, so it never allocates.
+// points make one cudaMalloc per device on first use (the status words). This entry point runs
+// the same CTA-pair tensor-core kernel with that scratch taken from a fixed, file-scope device
+// array instead, so it never allocates.
 //
-// What it costs. The array below (NOALLOC_SCRATCH_BYTES = 516 KiB) exists on every GPU that
+// What it costs. The array below (NOALLOC_SCRATCH_BYTES = 4 KiB) exists on every GPU that
 // loads this library, for the life of the process, whether or not this entry point is called.
 // All calls on a device share it and it keeps the last call's contents; the status words are
-// cleared (cudaMemsetAsync on the caller's stream) at the start of every call, the tensor-map
-// ring needs no clearing (each slot is written before it is read). Calls that overlap on the
-// GPU (different streams, no ordering between them) race on the status words.
+// cleared (cudaMemsetAsync on the caller's stream) at the start of every call. Calls that
+// overlap on the GPU (different streams, no ordering between them) race on the status words.
 #include <cudaTypedefs.h>
 
 #include <climits>
@@ -24,10 +23,7 @@
 
 namespace {
 
-constexpr int kSmIds = 256;            // SM identifiers the tensor-map ring covers
-constexpr size_t kStatusBytes = 4096;  // status words; the ring starts 4 KiB in (128-aligned)
-constexpr size_t kScratchBytes = kStatusBytes + static_cast<size_t>(kSmIds) * vark::TMAP_SLOTS *
-                                                    vark::TMAP_PAIR_BYTES;
+constexpr size_t kScratchBytes = 4096;  // status words
 static_assert(kScratchBytes == GGEMM_VARK_NOALLOC_SCRATCH_BYTES, "header and file disagree");
 
 // The scratch. In host code this name is only a stand-in for the device object: the device
@@ -67,7 +63,7 @@ int setup(Device** out) {
       return GGEMM_VARK_ECUDA;
     }
     if (major != 10 || minor != 0) return GGEMM_VARK_ENO_DEVICE;
-    if (d.sm_count > kSmIds || d.sm_count < 2) return GGEMM_VARK_ETOO_LARGE;
+    if (d.sm_count < 2) return GGEMM_VARK_ENO_DEVICE;  // the kernel runs on CTA pairs
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
       cudaGetLastError();
@@ -144,7 +140,7 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
   if (!aligned16(lhs) || !aligned16(rhs) || !aligned16(c) || stride_lhs_m % 16 != 0 ||
       stride_rhs_m % 16 != 0 || stride_cn != 1 || (2ll * stride_cm) % 16 != 0 ||
-      (2ll * stride_cg) % 16 != 0)
+      (2ll * stride_cg) % 16 != 0 || OUT_N % 8 != 0)  // TMA stores write 16-byte row pieces
     return GGEMM_VARK_ELAYOUT;
   if (G == 0) return GGEMM_VARK_OK;
 
@@ -156,9 +152,6 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   const int32_t col_tiles = (OUT_N + vark::PAIR_COLS - 1) / vark::PAIR_COLS;
   const int64_t items = static_cast<int64_t>(G) * row_tiles * col_tiles;
   if (items > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
-  // The scratch this call needs: the status words and one ring slice per SM identifier.
-  const size_t needed = kStatusBytes + vark::tc_tmap_ring_bytes(kSmIds);
-  if (needed > kScratchBytes) return GGEMM_VARK_ETOO_LARGE;
 
   const int64_t token_limit =
       m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
@@ -190,12 +183,6 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   tp.token_limit = token_limit;
   tp.status = st;
   tp.timeout_ns = kTimeoutNs;
-  tp.lhs = static_cast<const uint8_t*>(lhs);
-  tp.rhs = static_cast<const uint8_t*>(rhs);
-  tp.stride_lhs = stride_lhs_m;
-  tp.stride_rhs = stride_rhs_m;
-  tp.tmap_ring = d->scratch + kStatusBytes;
-  tp.num_sms = kSmIds;
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = stride_cg;
   tp.stride_cm = stride_cm;

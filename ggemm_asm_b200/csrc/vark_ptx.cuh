@@ -54,6 +54,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// The same wait with cluster-scope acquire: it pairs with a cluster-scope release arrive from the
+// peer CTA, so the peer's shared-memory writes before that arrive are visible afterwards.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // ---------------------------------------------------------------------------------------------
 // proxy fences
 // ---------------------------------------------------------------------------------------------
@@ -61,6 +75,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One warp: zero `bytes` (a multiple of 16) of shared memory from `saddr` (16-byte aligned).
+__device__ __forceinline__ void smem_zero_warp(uint32_t saddr, uint32_t bytes, int lane) {
+  for (uint32_t off = static_cast<uint32_t>(lane) * 16u; off < bytes; off += 32u * 16u)
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(saddr + off), "r"(0u)
+                 : "memory");
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -138,46 +159,6 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return p;
 }
 
-// ---------------------------------------------------------------------------------------------
-// Device-side tensor-map edits (a map is a 128-byte, 128-byte aligned object)
-// ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t sm_id() {
-  uint32_t id;
-  asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
-  return id;
-}
-
-__device__ __forceinline__ void tmap_set_address(uint32_t smem_map, uint64_t global_address) {
-  asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(
-                   smem_map),
-               "l"(global_address)
-               : "memory");
-}
-
-template <int ORD>
-__device__ __forceinline__ void tmap_set_dim(uint32_t smem_map, uint32_t extent) {
-  asm volatile("tensormap.replace.tile.global_dim.shared::cta.b1024.b32 [%0], %1, %2;" ::"r"(
-                   smem_map),
-               "n"(ORD), "r"(extent)
-               : "memory");
-}
-
-// Warp-collective: copy a map from shared to global memory and release it to the tensor-map
-// proxy.
-__device__ __forceinline__ void tmap_publish(void* gmem_map, uint32_t smem_map) {
-  asm volatile(
-      "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned"
-      " [%0], [%1], 128;" ::"l"(reinterpret_cast<uint64_t>(gmem_map)),
-      "r"(smem_map)
-      : "memory");
-}
-
-// Acquire a published map before this thread's first TMA that uses it.
-__device__ __forceinline__ void tmap_acquire(const void* gmem_map) {
-  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
-                   reinterpret_cast<uint64_t>(gmem_map))
-               : "memory");
-}
 
 // ---------------------------------------------------------------------------------------------
 // tcgen05 (5th-gen tensor core, tensor memory)
@@ -288,6 +269,14 @@ __device__ __forceinline__ void cluster_sync_all() {
 // purpose: a cluster-scope release here made each producer wait for its own in-flight TMA loads
 // before arriving, which halved the pair's load throughput. The data these barriers guard is
 // ordered by the TMA transaction count (loads) or by tcgen05 fences (TMEM), not by the arrive.
+// Arrive with cluster-scope release: this thread's earlier shared-memory writes (made visible to
+// the async proxy with fence_proxy_async_smem) are ordered before the arrive for a waiter that
+// acquires at cluster scope (mbar_try_wait_cluster).
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }

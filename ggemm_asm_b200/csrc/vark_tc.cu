@@ -21,14 +21,14 @@
 // The epilogue of one tile overlaps the MMAs of the next through the two accumulators.
 //
 // Variable K. A group's tokens [off_g, off_{g+1}) are walked in blocks of 128 that are aligned
-// to the END of the group, so only block 0 can be partial. Loads go through per-group tensor
-// maps built on the device: the producer copies the host-encoded maps into shared memory,
-// points them at row off_g with a token extent of K_g (tensormap.replace), and publishes them
-// to a per-SM ring in global memory. Block 0 then starts at the negative token coordinate
-// K_g - 128*nkb, and TMA fills the rows outside [0, K_g) with zeros without reading memory:
-// a neighbour's data (even Inf/NaN) never enters the sum, no load reaches past off_{g+1}, and
-// every stage is a uniform 4 MMAs (stages with fewer MMAs stall the recycled-stage pipeline
-// on this hardware). Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
+// to the START of the group, through the launch's own tensor maps over all M_total tokens (no
+// map is built on the device). Only the last block can hold rows that are not the group's
+// (another group's tokens, or TMA zero fill past M_total). That block completes on a second
+// barrier; the producer zeroes those rows in every box of the stage (all operands, so that a
+// neighbour's Inf or NaN never meets a zero and enters the sum as NaN), makes the writes visible
+// to the tensor core (proxy fence) and then releases the stage to the MMA warp. Every stage is
+// a uniform 4 MMAs (stages with fewer MMAs stall the recycled-stage pipeline on this hardware).
+// Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA sets the abort
 // flag and GGEMM_VARK_DEV_TIMEOUT in the status block, every role leaves its loop, in-flight
@@ -65,14 +65,13 @@ constexpr uint32_t OFF_RHS = 0;
 constexpr uint32_t OFF_LHS = OFF_RHS + STAGES * RHS_STAGE_BYTES;
 constexpr uint32_t OFF_EPI = OFF_LHS + STAGES * LHS_STAGE_BYTES;
 constexpr uint32_t OFF_ZERO = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t OFF_TMAP = OFF_ZERO + EPI_BUF_BYTES;             // 2 x 128 B, 128-aligned
-constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
-constexpr uint32_t NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+constexpr uint32_t OFF_BARS = OFF_ZERO + EPI_BUF_BYTES;
+constexpr uint32_t NUM_BARS = 2 * STAGES + 2 + 2 + 1 + 1;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
 constexpr uint32_t SMEM_USED = OFF_MISC + 16;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;  // alignment slack
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
-static_assert(OFF_TMAP % 128 == 0, "tensor maps must be 128-byte aligned");
+static_assert(OFF_BARS % 8 == 0, "mbarriers are 8-byte aligned");
 
 constexpr uint32_t IDESC = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
                                         /*A MN-major*/ 1, /*B MN-major*/ 1, 128, TILE_ROWS);
@@ -154,6 +153,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t bar_tfull = bar_empty + 8 * STAGES;         // [2]
   const uint32_t bar_tempty = bar_tfull + 16;                // [2]
   const uint32_t bar_drain = bar_tempty + 16;                // [1]
+  const uint32_t bar_zfill = bar_drain + 8;                  // [1] a group's last block
   uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(sbase + OFF_MISC + 4);
 
@@ -174,7 +174,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(bar_tempty + 8 * a, EPI_WARPS);
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_zfill, 1);
     fence_mbar_init();
+    tma_prefetch_desc(&map_rhs);
+    tma_prefetch_desc(&map_lhs);
     tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
@@ -192,69 +195,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ======================= TMA producer (lane 0 issues; the warp stays converged) ==========
     const uint64_t policy = l2_policy_evict_last();
-    const uint32_t smid = sm_id();
     // Failure-detection test hook (GGEMM_VARK_TEST_STALL_MAGIC): withhold the first stage.
     bool withhold =
         p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
                                    GGEMM_VARK_TEST_STALL_MAGIC;
-    const uint32_t smem_maps = base + OFF_TMAP;
-    uint32_t stage = 0, phase = 0;
+    uint32_t stage = 0, phase = 0, zphase = 0;
     uint32_t used_mask = 0, parity_mask = 0;  // per stage: issued at least once / last parity
-    int cur_group = -1;
-    uint32_t slot = 0;
-    const CUtensorMap* gmap_rhs = nullptr;
-    const CUtensorMap* gmap_lhs = nullptr;
-    bool ok = smid < static_cast<uint32_t>(p.num_sms);
-    if (!ok && lane == 0) report_timeout(ctl, 0x500u);  // ring too small: refuse to run
+    bool ok = true, zpending = false;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const TileInfo t = decode_tile(p, tile, false);
       if (t.tokens == 0) continue;
-      if (t.g != cur_group) {
-        // Per-group maps: base at row off_g, token extent K_g, into the next ring slot.
-        slot = (slot + 1) % TMAP_SLOTS;
-        uint8_t* const pair =
-            p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
-        if (lane < 16) {
-          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_rhs : &map_lhs);
-          reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
-        }
-        __syncwarp();
-        if (lane == 0) {
-          const int64_t lo = t.end - t.tokens;
-          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
-          tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
-          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
-          tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
-        }
-        __syncwarp();
-        tmap_publish(pair, smem_maps);
-        tmap_publish(pair + 128, smem_maps + 128);
-        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair);
-        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
-        if (lane == 0) {
-          tmap_acquire(gmap_rhs);
-          tmap_acquire(gmap_lhs);
-        }
-        __syncwarp();
-        cur_group = t.g;
-      }
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
-      const int32_t y0 = t.tokens - TILE_TOKENS * nkb;  // <= 0: rows before the group read as 0
+      const int rem = t.tokens - TILE_TOKENS * (nkb - 1);  // the group's tokens in its last block
+      // First token of the group as a TMA row coordinate (token_limit <= INT32_MAX).
+      const int32_t lo = static_cast<int32_t>(t.end - t.tokens);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
           ok = false;
           break;
         }
-        if (lane == 0 && !withhold) {
-          const uint32_t fb = bar_full + 8 * stage;
-          mbar_arrive_expect_tx(fb, STAGE_TX_BYTES);
-          const int32_t y = y0 + TILE_TOKENS * kb;
-          tma_load_2d_hint(base + OFF_RHS + stage * RHS_STAGE_BYTES, gmap_rhs, fb, t.col0, y,
-                           policy);
+        const uint32_t fb = bar_full + 8 * stage;
+        const uint32_t rhs_dst = base + OFF_RHS + stage * RHS_STAGE_BYTES;
+        const uint32_t lhs_dst = base + OFF_LHS + stage * LHS_STAGE_BYTES;
+        const int32_t y = lo + TILE_TOKENS * kb;
+        const bool last_partial = kb == nkb - 1 && rem < TILE_TOKENS;
+        if (!withhold) {
+          // A group's last, partial block lands on bar_zfill instead: its rows [rem, 128) are
+          // zeroed before the stage is released to the MMA warp.
+          const uint32_t lb = last_partial ? bar_zfill : fb;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(lb, STAGE_TX_BYTES);
+            tma_load_2d_hint(rhs_dst, &map_rhs, lb, t.col0, y, policy);
 #pragma unroll
-          for (int b = 0; b < LHS_BOXES; ++b)
-            tma_load_2d_hint(base + OFF_LHS + stage * LHS_STAGE_BYTES + b * LHS_BOX_BYTES,
-                             gmap_lhs, fb, t.row0 + 128 * b, y, policy);
+            for (int b = 0; b < LHS_BOXES; ++b)
+              tma_load_2d_hint(lhs_dst + b * LHS_BOX_BYTES, &map_lhs, lb, t.row0 + 128 * b, y,
+                               policy);
+          }
+          if (last_partial) {
+            zpending = true;
+            if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) {
+              ok = false;
+              break;
+            }
+            zpending = false;
+            zphase ^= 1u;
+            // Whole 128-byte token rows, so the 128-byte swizzle does not matter.
+            const uint32_t keep = static_cast<uint32_t>(rem) * 128u;
+            smem_zero_warp(rhs_dst + keep, RHS_STAGE_BYTES - keep, lane);
+#pragma unroll
+            for (int b = 0; b < LHS_BOXES; ++b)
+              smem_zero_warp(lhs_dst + b * LHS_BOX_BYTES + keep, LHS_BOX_BYTES - keep, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(fb);
+          }
         }
         __syncwarp();
         withhold = false;
@@ -274,6 +268,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t par = (parity_mask >> s) & 1u;
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(bar_full + 8 * s, par)) {
+          if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
+        }
+      }
+      if (zpending) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_zfill, zphase)) {
           if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
         }
       }

@@ -39,11 +39,14 @@
 // The leader's commits arrive on both CTAs' barriers (tcgen05.commit multicast); the epilogue
 // warps of both CTAs release an accumulator on the leader's barrier.
 //
-// Variable K. As in the single-CTA kernel (vark_tc.cu): token blocks aligned to the END of the
-// group, loads through per-group tensor maps built on the device (base at row off_g, token
-// extent K_g), so the partial first block starts at a negative coordinate and TMA fills the
-// rows before the group with zeros; every stage is a uniform TK/32 MMAs. Empty groups skip the
-// pipeline and the epilogue stores zeros.
+// Variable K. Loads go through the launch's own tensor maps over all M_total tokens (no map is
+// built on the device). A group's tokens [off_g, off_{g+1}) are walked in blocks of TK aligned
+// to the group's START, so only the last block can hold tokens of other groups (or TMA zero
+// fill past M_total). That block is loaded into each CTA's own barrier; the producer then zeroes
+// its rows past the group in both boxes (both, so that an Inf or NaN in a neighbour's token can
+// never meet a zero and enter the sum as NaN), makes the writes visible to the tensor core
+// (proxy fence) and releases the stage to the leader at cluster scope. Every stage is a uniform
+// TK/32 MMAs. Empty groups skip the pipeline and the epilogue stores zeros.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
 // GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs of the pair, every role leaves its
@@ -87,14 +90,13 @@ static_assert(TK % 32 == 0 && TK >= 64 && TK <= 256, "token block: a multiple of
 constexpr uint32_t OFF_RHS = 0;                          // operand A stages
 constexpr uint32_t OFF_LHS = OFF_RHS + ST * BOX_BYTES;   // operand B stages
 constexpr uint32_t OFF_EPI = OFF_LHS + ST * BOX_BYTES;
-constexpr uint32_t OFF_TMAP = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t OFF_BARS = OFF_TMAP + 2 * 128;
-constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1;
+constexpr uint32_t OFF_BARS = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
+constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1 + 1;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
 constexpr uint32_t SMEM_USED = OFF_MISC + 16;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
-static_assert(OFF_TMAP % 128 == 0 && OFF_EPI % 1024 == 0, "alignment");
+static_assert(OFF_EPI % 1024 == 0, "alignment");
 
 // Instruction descriptors without N: the item's N is or-ed in at run time.
 constexpr uint32_t IDESC_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
@@ -118,13 +120,18 @@ __device__ __noinline__ void report_timeout(const Ctl& ctl, uint32_t where) {
   }
 }
 
-// Bounded wait by every lane of a warp; warp-uniform verdict (see vark_tc.cu).
+// Bounded wait by every lane of a warp; warp-uniform verdict (see vark_tc.cu). CLUSTER: acquire
+// at cluster scope (a stage the peer CTA wrote with generic stores).
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool warp_wait(const Ctl& ctl, uint32_t bar, uint32_t parity,
                                           uint32_t where) {
-  bool ok = mbar_try_wait(bar, parity);
+  auto try_wait = [&] {
+    return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  bool ok = try_wait();
   if (!ok) {
     const uint64_t t0 = globaltimer_ns();
-    while (!(ok = mbar_try_wait(bar, parity))) {
+    while (!(ok = try_wait())) {
       if (*ctl.abort) break;
       if (globaltimer_ns() - t0 > ctl.timeout_ns) {
         report_timeout(ctl, where);
@@ -186,6 +193,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t bar_tfull = bar_empty + 8 * ST;     // [2]   both CTAs
   const uint32_t bar_tempty = bar_tfull + 16;        // [2]   used in the leader only
   const uint32_t bar_drain = bar_tempty + 16;        // [1]   leader
+  const uint32_t bar_zfill = bar_drain + 8;          // [1]   both CTAs: a group's last block
   uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(sbase + OFF_MISC + 4);
 
@@ -201,7 +209,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(bar_tempty + 8 * a, 2 * EPI_WARPS);   // every epilogue warp of the pair
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_zfill, 1);  // this CTA's producer
     fence_mbar_init();
+    tma_prefetch_desc(&map_lhs);
+    tma_prefetch_desc(&map_rhs);
     tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
@@ -222,73 +233,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) =======================================
     const uint64_t policy = l2_policy_evict_last();
-    const uint32_t smid = sm_id();
     // Failure-detection test hook (GGEMM_VARK_TEST_STALL_MAGIC): withhold the first stage.
     bool withhold =
         p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
                                    GGEMM_VARK_TEST_STALL_MAGIC;
-    const uint32_t smem_maps = base + OFF_TMAP;
-    uint32_t stage = 0, phase = 0;
-    int cur_group = -1;
-    uint32_t slot = 0;
-    const CUtensorMap* gmap_lhs = nullptr;
-    const CUtensorMap* gmap_rhs = nullptr;
-    bool ok = smid < static_cast<uint32_t>(p.num_sms);
-    if (!ok && lane == 0) report_timeout(ctl, 0x500u);
+    uint32_t stage = 0, phase = 0, zphase = 0;
+    bool ok = true, zpending = false;
     Item nxt = decode_item(p, cluster, false);
     for (int item = cluster; item < num_items && ok; item += nclusters) {
       const Item t = nxt;  // decoded one item ahead: the offsets' load latency is hidden
       if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
       if (t.tokens == 0) continue;
-      if (t.g != cur_group) {
-        slot = (slot + 1) % TMAP_SLOTS;
-        uint8_t* const pair =
-            p.tmap_ring + (static_cast<size_t>(smid) * TMAP_SLOTS + slot) * TMAP_PAIR_BYTES;
-        if (lane < 16) {
-          const uint4* src = reinterpret_cast<const uint4*>(lane < 8 ? &map_rhs : &map_lhs);
-          reinterpret_cast<uint4*>(sbase + OFF_TMAP)[lane] = src[lane & 7];
-        }
-        __syncwarp();
-        if (lane == 0) {
-          const int64_t lo = t.end - t.tokens;
-          tmap_set_address(smem_maps, reinterpret_cast<uint64_t>(p.rhs + lo * p.stride_rhs));
-          tmap_set_dim<1>(smem_maps, static_cast<uint32_t>(t.tokens));
-          tmap_set_address(smem_maps + 128, reinterpret_cast<uint64_t>(p.lhs + lo * p.stride_lhs));
-          tmap_set_dim<1>(smem_maps + 128, static_cast<uint32_t>(t.tokens));
-        }
-        __syncwarp();
-        tmap_publish(pair, smem_maps);
-        tmap_publish(pair + 128, smem_maps + 128);
-        gmap_rhs = reinterpret_cast<const CUtensorMap*>(pair);
-        gmap_lhs = reinterpret_cast<const CUtensorMap*>(pair + 128);
-        if (lane == 0) {
-          tmap_acquire(gmap_lhs);
-          tmap_acquire(gmap_rhs);
-        }
-        __syncwarp();
-        cur_group = t.g;
-      }
       const int nkb = (t.tokens + TK - 1) / TK;
-      const int32_t y0 = t.tokens - TK * nkb;  // <= 0: rows before the group read as zeros
+      const int rem = t.tokens - TK * (nkb - 1);  // the group's tokens in its last block
+      // First token of the group as a TMA row coordinate (token_limit <= INT32_MAX).
+      const int32_t lo = static_cast<int32_t>(t.end - t.tokens);
       // A: this CTA's 128 C columns (RHS); B: this CTA's half of the item's rows (LHS). Edge
       // items swap them: A = 128 C rows (LHS), B = half of the edge columns (RHS). Every N/2 is
       // a multiple of 16, so the TMA x coordinates stay 16-byte aligned.
       const int32_t r = static_cast<int32_t>(rank);
       const int32_t xa = t.edge ? t.m0 + PAIR_HALF * r : t.n0 + PAIR_HALF * r;
       const int32_t xb = t.edge ? t.n0 + (t.ecols >> 1) * r : t.m0 + (t.nrows >> 1) * r;
-      const CUtensorMap* const map_a = t.edge ? gmap_lhs : gmap_rhs;
-      const CUtensorMap* const map_b = t.edge ? gmap_rhs : gmap_lhs;
+      const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
+      const CUtensorMap* const map_b = t.edge ? &map_rhs : &map_lhs;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
           ok = false;
           break;
         }
-        if (lane == 0 && !withhold) {
-          const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
-          mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
-          const int32_t y = y0 + TK * kb;
-          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, map_a, fb, xa, y, policy);
-          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, map_b, fb, xb, y, policy);
+        const uint32_t a_dst = base + OFF_RHS + stage * BOX_BYTES;
+        const uint32_t b_dst = base + OFF_LHS + stage * BOX_BYTES;
+        const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
+        const int32_t y = lo + TK * kb;
+        if (withhold) {
+          // nothing issued: the leader's wait on this stage runs out
+        } else if (kb < nkb - 1 || rem == TK) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
+            tma_load_2d_pair(a_dst, map_a, fb, xa, y, policy);
+            tma_load_2d_pair(b_dst, map_b, fb, xb, y, policy);
+          }
+        } else {
+          // The group's last, partial block: rows [rem, TK) are not the group's. Load into this
+          // CTA's own barrier, zero those rows of both boxes (whole 128-byte rows, so the swizzle
+          // does not matter), then release the stage to the leader.
+          if (lane == 0) {
+            mbar_arrive_expect_tx(bar_zfill, STAGE_BYTES);
+            tma_load_2d_hint(a_dst, map_a, bar_zfill, xa, y, policy);
+            tma_load_2d_hint(b_dst, map_b, bar_zfill, xb, y, policy);
+          }
+          zpending = true;
+          if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) {
+            ok = false;
+            break;
+          }
+          zpending = false;
+          zphase ^= 1u;
+          const uint32_t keep = static_cast<uint32_t>(rem) * 128u;
+          smem_zero_warp(a_dst + keep, BOX_BYTES - keep, lane);
+          smem_zero_warp(b_dst + keep, BOX_BYTES - keep, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_release_cluster(fb);
         }
         __syncwarp();
         withhold = false;
@@ -300,7 +306,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     // Loads still in flight are drained through the empty barriers: every stage this producer
     // filled is released by the leader's commit once its MMAs (which waited for the data)
-    // finish; after an abort the wait is bounded.
+    // finish; a last block whose wait was cut short is drained on its own barrier. After an
+    // abort the waits are bounded.
     if (lane == 0) {
       for (int s = 0; s < ST; ++s) {
         const uint64_t t0 = globaltimer_ns();
@@ -308,6 +315,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // parity. Waiting for "phase ^ 1" of the CURRENT position covers the stages ahead.
         const uint32_t par = (static_cast<uint32_t>(s) < stage) ? phase : (phase ^ 1u);
         while (!mbar_try_wait(bar_empty + 8 * s, par)) {
+          if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
+        }
+      }
+      if (zpending) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_zfill, zphase)) {
           if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
         }
       }
@@ -325,13 +338,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
         if (t.tokens == 0) continue;
         const int nkb = (t.tokens + TK - 1) / TK;
+        const bool partial = t.tokens % TK != 0;  // the last block was zeroed by generic stores
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
         const uint32_t idesc = t.edge ? IDESC_EDGE_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
                                       : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
+          const uint32_t full = bar_full + 8 * stage;
+          const bool landed = (partial && kb == nkb - 1)
+                                  ? warp_wait<true>(ctl, full, phase, 0x300u | stage)
+                                  : warp_wait(ctl, full, phase, 0x300u | stage);
+          if (!landed) {
             ok = false;
             break;
           }

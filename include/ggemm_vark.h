@@ -137,14 +137,13 @@ GGEMM_VARK_API int ggemm_vark_tc_supported(const void* lhs, const void* rhs, voi
  * (every device byte must come from the pool), allocators with strict accounting, processes that
  * fixed their device footprint up front, and latency-critical paths that must not hit the
  * implicit synchronisation of cudaMalloc/cudaFree. This entry point runs the tensor-core (CTA
- * pair) kernel with its scratch - status words and the per-SM ring of tensor maps the kernel
- * builds - taken from a file-scope device array of GGEMM_VARK_NOALLOC_SCRATCH_BYTES (516 KiB)
- * that every GPU loading this library holds until the process exits. It never calls cudaMalloc
- * or cudaFree.
+ * pair) kernel with its scratch - the status words - taken from a file-scope device array of
+ * GGEMM_VARK_NOALLOC_SCRATCH_BYTES (4 KiB) that every GPU loading this library holds until the
+ * process exits. It never calls cudaMalloc or cudaFree.
  *
  *  - Arguments as ggemm_vark_fp8_wgrad_ex; only tensor-core layouts are accepted (16-byte
- *    aligned bases and row pitches, stride_cn == 1), anything else returns GGEMM_VARK_ELAYOUT,
- *    and a device whose SM count the scratch does not cover returns GGEMM_VARK_ETOO_LARGE.
+ *    aligned bases and row pitches, stride_cn == 1, OUT_N a multiple of 8), anything else
+ *    returns GGEMM_VARK_ELAYOUT.
  *  - `status`: a caller-owned 16-byte aligned device buffer for the GGEMM_VARK_DEV_* bits, or
  *    NULL to record them in the shared array (cleared at the start of every call, not readable).
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
@@ -152,7 +151,7 @@ GGEMM_VARK_API int ggemm_vark_tc_supported(const void* lhs, const void* rhs, voi
  *  - All calls on a device share the array and it keeps the last call's contents; calls that
  *    overlap on the GPU (different streams without ordering) race on its status words.
  */
-#define GGEMM_VARK_NOALLOC_SCRATCH_BYTES 528384u
+#define GGEMM_VARK_NOALLOC_SCRATCH_BYTES 4096u
 GGEMM_VARK_API int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, void* c,
                             const float* lhs_scale, const float* rhs_scale,
                             const int64_t* group_offs,

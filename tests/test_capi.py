@@ -104,6 +104,8 @@ def test_valid_call_without_device_reports_no_device():
     (dict(), 1),
     (dict(lhs=P + 1), 0), (dict(c=P + 8), 0), (dict(slm=72), 0), (dict(srm=136), 0), (dict(srm=144), 1),
     (dict(scn=2), 0), (dict(scm=132), 0), (dict(scm=136), 1), (dict(scg=64 * 128 + 4), 0),
+    # a TMA store writes C rows in 16-byte pieces: OUT_N must be a multiple of 8 elements
+    (dict(N=124), 0), (dict(N=120), 1), (dict(N=4), 0),
 ])
 def test_tensor_core_layout_rules(kw, expect):
     a = dict(lhs=P, rhs=P, c=P, M=64, N=128, slm=64, srm=128, scg=64 * 128, scm=128, scn=1)

@@ -185,6 +185,64 @@ def test_fwd_rows_outside_experts_untouched():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("trans_b", [True, False])
+@pytest.mark.parametrize("N", [20, 100])
+def test_fwd_ragged_rows_and_columns_stay_inside(trans_b, N):
+    """Experts that end inside a 32-row chunk (their last rows are written with plain stores,
+    clipped to the expert) and N not a multiple of 8 (the last piece of a row is written element
+    by element): results match the oracle, and a sentinel survives in the padding columns of C
+    and in the rows outside the experts."""
+    lens, K, lead, tail = [45, 0, 290, 7, 131, 1], 160, 3, 5
+    a, b, sa, sb, _ = make_fwd(lens, N, K, seed=N + 17, per_expert_scale=True)
+    M, G = sum(lens), len(lens)
+    a_all = torch.cat([torch.zeros(lead, K), a.float(), torch.zeros(tail, K)]).to(a.dtype)
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens)) + lead
+    pitch = (N + 7) // 8 * 8 + 8
+    out = torch.full((lead + M + tail, pitch), 7.0, dtype=torch.bfloat16, device="cuda")
+    if trans_b:
+        bl, bd = b, b.cuda()
+    else:
+        bl = b.transpose(1, 2).contiguous()  # [G, K, N]
+        npad = (N + 15) // 16 * 16           # B rows of a [G, K, N] weight: 16-byte pitch
+        bd = torch.zeros(G, K, npad, dtype=torch.uint8, device="cuda")
+        bd[:, :, :N] = bl.view(torch.uint8).cuda()
+        bd = bd.view(E4M3)[:, :, :N]
+    grouped_gemm_fp8_tensorwise(a_all.cuda(), bd, sa.cuda(), sb.cuda(), offs.cuda(),
+                                trans_b=trans_b, out=out[:, :N])
+    torch.cuda.synchronize()
+    o = out.cpu()
+    assert bool((o[:, N:] == 7).all()), "padding columns written"
+    assert bool((o[:lead] == 7).all()) and bool((o[lead + M:] == 7).all()), "rows outside written"
+    check(a_all, bl, sa, sb, offs, o[:, :N], torch.arange(lead, lead + M), trans_b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("trans_b", [True, False])
+@pytest.mark.parametrize("K", [20, 100])
+def test_fwd_k_padding_is_not_read(trans_b, K):
+    """K not a multiple of 16 with padded rows full of large values: the K tail of the last
+    stage must read as zero (TMA fill), so the padding never enters the sums."""
+    lens, N = [70, 0, 300, 33], 96
+    a, b, sa, sb, offs = make_fwd(lens, N, K, seed=K + 31)
+    M, G = sum(lens), len(lens)
+    junk = 0x7E  # e4m3fn 448: any padding byte read into a sum moves it far out of tolerance
+    kp = (K + 15) // 16 * 16 + 16
+    ap = torch.full((M, kp), junk, dtype=torch.uint8)
+    ap[:, :K] = a.view(torch.uint8)
+    ad = ap.cuda().view(E4M3)[:, :K]
+    if trans_b:
+        bp = torch.full((G, N, kp), junk, dtype=torch.uint8)
+        bp[:, :, :K] = b.view(torch.uint8)
+        bd, bl = bp.cuda().view(E4M3)[:, :, :K], b
+    else:
+        bl = b.transpose(1, 2).contiguous()  # [G, K, N]; its rows are whole N, K is the row index
+        bd = bl.cuda()
+    got = grouped_gemm_fp8_tensorwise(ad, bd, sa.cuda(), sb.cuda(), offs.cuda(), trans_b=trans_b)
+    torch.cuda.synchronize()
+    check(a, bl, sa, sb, offs, got, trans_b=trans_b)
+
+
+@pytest.mark.gpu
 def test_fwd_padded_strides_and_14_arg_entry():
     lens, N, K = [333, 222], 272, 320
     a, b, sa, sb, offs = make_fwd(lens, N, K, seed=9)

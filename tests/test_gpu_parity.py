@@ -75,8 +75,10 @@ def test_ragged_groups(lens, path):
 
 @pytest.mark.parametrize("shape", [(240, 128), (480, 256), (16, 16), (2880, 128), (64, 5760),
                                    (496, 400), (256, 256), (272, 272), (128, 640),
-                                   # last column tile widths 64, 96, 224, 32 (transposed items)
-                                   (2880, 2880), (112, 96), (304, 480), (48, 224), (512, 32)])
+                                   # last column tile widths 64, 96, 224, 32, 192 (transposed
+                                   # items; 256 x 192 is the MoE layer test's weight gradient)
+                                   (2880, 2880), (112, 96), (304, 480), (48, 224), (512, 32),
+                                   (256, 192)])
 @pytest.mark.parametrize("path", TC_PATHS)
 def test_tile_edges(shape, path):
     OUT_M, OUT_N = shape
@@ -111,19 +113,29 @@ def test_launcher_closed_form(path):
         assert bool((out[g] == expect).all()), (g, out[g].unique()[:4], expect)
 
 
+@pytest.mark.parametrize("where", ["middle group", "after the last group"])
 @pytest.mark.parametrize("path", TC_PATHS)
-def test_neighbour_nan_does_not_leak(path):
-    """Rows before a group's start are never read: per-group tensor maps zero-fill them."""
+def test_neighbour_nan_does_not_leak(path, where):
+    """Tokens that are not a group's own never enter its sum, even as NaN or Inf in both
+    operands: a group's last token block reaches into the next group's rows (or rows past the
+    last group) and the kernel zeroes those rows in both operands before the MMA."""
     p = inputs.make_problem("tiny", seed=13, lens=[100, 50, 200], OUT_M=240, OUT_N=128)
     lhs = p.lhs.view(torch.uint8).clone()
     rhs = p.rhs.view(torch.uint8).clone()
-    lhs[:100] = 0x7F  # e4m3fn NaN
-    rhs[:100] = 0x7C  # e5m2 +Inf
+    if where == "middle group":
+        lhs[100:150] = 0x7F  # e4m3fn NaN
+        rhs[100:150] = 0x7C  # e5m2 +Inf
+        clean = [0, 2]
+    else:  # 300 poisoned rows after offs[G]; the operands (and m_total) include them
+        lhs = torch.cat([lhs, torch.full((300, lhs.shape[1]), 0x7F, dtype=torch.uint8)])
+        rhs = torch.cat([rhs, torch.full((300, rhs.shape[1]), 0x7C, dtype=torch.uint8)])
+        clean = [0, 1, 2]
     q = inputs.Problem(**{**p.__dict__, "lhs": lhs.view(torch.float8_e4m3fn),
                           "rhs": rhs.view(torch.float8_e5m2)})
     out = _run(q, path)
-    assert bool(torch.isnan(out[0].float()).any() or torch.isinf(out[0].float()).any())
-    _check(q, out, groups=[1, 2], label="nan-neighbour")
+    if where == "middle group":
+        assert bool(torch.isnan(out[1].float()).any() or torch.isinf(out[1].float()).any())
+    _check(q, out, groups=clean, label=f"nan-neighbour/{where}")
 
 
 @pytest.mark.parametrize("path", TC_PATHS)
@@ -150,6 +162,27 @@ def test_unaligned_layout_takes_simt():
     out = vark(lhs_view, d.rhs, d.lhs_scale, d.rhs_scale, d.group_offs)  # auto -> SIMT
     torch.cuda.synchronize()
     _check(p, out, label="unaligned")
+
+
+def test_ragged_out_n_keeps_padding_columns():
+    """OUT_N not a multiple of 8 with a padded C pitch: a TMA store would write the row up to the
+    next 16-byte boundary, so the tensor-core paths refuse the layout and auto takes the CUDA-core
+    path; the caller's columns past OUT_N keep their contents."""
+    p = inputs.make_problem("tiny", seed=29, lens=[200, 0, 77, 300], OUT_M=96, OUT_N=124)
+    d = p.to("cuda")
+    wide_r = torch.zeros(d.rhs.shape[0], 128, dtype=torch.uint8, device="cuda")
+    wide_r[:, :124] = d.rhs.view(torch.uint8)
+    rhs = wide_r[:, :124].view(torch.float8_e5m2)  # 16-byte row pitch: only OUT_N is ragged
+    big = torch.full((4, 96, 136), 7.0, dtype=torch.bfloat16, device="cuda")
+    view = big[:, :, :124]
+    for path in TC_PATHS:
+        with pytest.raises(_lib.VarkError) as ei:
+            vark(d.lhs, rhs, d.lhs_scale, d.rhs_scale, d.group_offs, path=path, out=view)
+        assert ei.value.code == _lib.ELAYOUT
+    vark(d.lhs, rhs, d.lhs_scale, d.rhs_scale, d.group_offs, out=view)
+    torch.cuda.synchronize()
+    assert bool((big[:, :, 124:] == 7.0).all())
+    _check(p, view, label="ragged OUT_N")
 
 
 @pytest.mark.parametrize("path", TC_PATHS)

@@ -238,7 +238,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
                                    GGEMM_VARK_TEST_STALL_MAGIC;
     uint32_t stage = 0, phase = 0, zphase = 0;
-    bool ok = true, zpending = false;
+    bool ok = true;
+    // A group's last block whose rows past the group still have to be zeroed (-1: none). Its
+    // zeroing is finished at the producer's next stop, after the following stage's empty wait:
+    // by then the block has usually landed, and the MMA warp still has the stages before it.
+    int zstage = -1;
+    uint32_t zkeep = 0;
+    auto finish_zfill = [&]() -> bool {
+      if (zstage < 0) return true;
+      if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) return false;
+      zphase ^= 1u;
+      const uint32_t zs = static_cast<uint32_t>(zstage);
+      smem_zero_warp(base + OFF_RHS + zs * BOX_BYTES + zkeep, BOX_BYTES - zkeep, lane);
+      smem_zero_warp(base + OFF_LHS + zs * BOX_BYTES + zkeep, BOX_BYTES - zkeep, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_release_cluster(mapa_shared(bar_full + 8 * zs, 0));
+      zstage = -1;
+      return true;
+    };
     Item nxt = decode_item(p, cluster, false);
     for (int item = cluster; item < num_items && ok; item += nclusters) {
       const Item t = nxt;  // decoded one item ahead: the offsets' load latency is hidden
@@ -257,7 +275,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
       const CUtensorMap* const map_b = t.edge ? &map_rhs : &map_lhs;
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
+        // The empty wait does not depend on a pending last block: this stage's previous fill
+        // is ST - 1 stages older than that block in the MMA warp's order.
+        if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage) ||
+            !finish_zfill()) {
           ok = false;
           break;
         }
@@ -274,27 +295,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             tma_load_2d_pair(b_dst, map_b, fb, xb, y, policy);
           }
         } else {
-          // The group's last, partial block: rows [rem, TK) are not the group's. Load into this
-          // CTA's own barrier, zero those rows of both boxes (whole 128-byte rows, so the swizzle
-          // does not matter), then release the stage to the leader.
+          // The group's last, partial block: rows [rem, TK) are not the group's. It lands on this
+          // CTA's own barrier; finish_zfill later zeroes those rows of both boxes (whole 128-byte
+          // rows, so the swizzle does not matter) and releases the stage to the leader.
           if (lane == 0) {
             mbar_arrive_expect_tx(bar_zfill, STAGE_BYTES);
             tma_load_2d_hint(a_dst, map_a, bar_zfill, xa, y, policy);
             tma_load_2d_hint(b_dst, map_b, bar_zfill, xb, y, policy);
           }
-          zpending = true;
-          if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) {
-            ok = false;
-            break;
-          }
-          zpending = false;
-          zphase ^= 1u;
-          const uint32_t keep = static_cast<uint32_t>(rem) * 128u;
-          smem_zero_warp(a_dst + keep, BOX_BYTES - keep, lane);
-          smem_zero_warp(b_dst + keep, BOX_BYTES - keep, lane);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_release_cluster(fb);
+          zstage = static_cast<int>(stage);
+          zkeep = static_cast<uint32_t>(rem) * 128u;
         }
         __syncwarp();
         withhold = false;
@@ -304,10 +314,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    if (ok && !finish_zfill()) ok = false;
     // Loads still in flight are drained through the empty barriers: every stage this producer
     // filled is released by the leader's commit once its MMAs (which waited for the data)
-    // finish; a last block whose wait was cut short is drained on its own barrier. After an
+    // finish; a last block still pending after an abort is drained on its own barrier. After an
     // abort the waits are bounded.
+    const bool zpending = zstage >= 0;
     if (lane == 0) {
       for (int s = 0; s < ST; ++s) {
         const uint64_t t0 = globaltimer_ns();

@@ -42,11 +42,14 @@
 // Variable K. Loads go through the launch's own tensor maps over all M_total tokens (no map is
 // built on the device). A group's tokens [off_g, off_{g+1}) are walked in blocks of TK aligned
 // to the group's START, so only the last block can hold tokens of other groups (or TMA zero
-// fill past M_total). That block is loaded into each CTA's own barrier; the producer then zeroes
-// its rows past the group in both boxes (both, so that an Inf or NaN in a neighbour's token can
-// never meet a zero and enter the sum as NaN), makes the writes visible to the tensor core
-// (proxy fence) and releases the stage to the leader at cluster scope. Every stage is a uniform
-// TK/32 MMAs. Empty groups skip the pipeline and the epilogue stores zeros.
+// fill past M_total). The MMA warp issues only the K steps (32 tokens) of that block that hold
+// group tokens. When the group ends inside a step, that step's rows past the group must be
+// zero: the block is loaded onto the CTA's own barrier, and at its next stop (after the
+// following stage's empty wait, when the block has usually landed) the producer zeroes those
+// rows in both boxes (both, so that an Inf or NaN in a neighbour's token can never meet a zero
+// and enter the sum as NaN), makes the writes visible to the tensor core (proxy fence) and
+// releases the stage to the leader at cluster scope; the MMA warp waits for such a stage with a
+// cluster-scope acquire. Empty groups skip the pipeline and the epilogue stores zeros.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
 // GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs of the pair, every role leaves its
@@ -243,14 +246,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // zeroing is finished at the producer's next stop, after the following stage's empty wait:
     // by then the block has usually landed, and the MMA warp still has the stages before it.
     int zstage = -1;
-    uint32_t zkeep = 0;
+    uint32_t zkeep = 0, zend = 0;
     auto finish_zfill = [&]() -> bool {
       if (zstage < 0) return true;
       if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) return false;
       zphase ^= 1u;
       const uint32_t zs = static_cast<uint32_t>(zstage);
-      smem_zero_warp(base + OFF_RHS + zs * BOX_BYTES + zkeep, BOX_BYTES - zkeep, lane);
-      smem_zero_warp(base + OFF_LHS + zs * BOX_BYTES + zkeep, BOX_BYTES - zkeep, lane);
+      smem_zero_warp(base + OFF_RHS + zs * BOX_BYTES + zkeep, zend - zkeep, lane);
+      smem_zero_warp(base + OFF_LHS + zs * BOX_BYTES + zkeep, zend - zkeep, lane);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive_release_cluster(mapa_shared(bar_full + 8 * zs, 0));
@@ -288,16 +291,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int32_t y = lo + TK * kb;
         if (withhold) {
           // nothing issued: the leader's wait on this stage runs out
-        } else if (kb < nkb - 1 || rem == TK) {
+        } else if (kb < nkb - 1 || (rem & 31) == 0) {
+          // (a last block that ends on a 32-token step: the MMA warp issues only rem / 32 steps,
+          // so the rows past the group are never multiplied)
           if (lane == 0) {
             mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
             tma_load_2d_pair(a_dst, map_a, fb, xa, y, policy);
             tma_load_2d_pair(b_dst, map_b, fb, xb, y, policy);
           }
         } else {
-          // The group's last, partial block: rows [rem, TK) are not the group's. It lands on this
-          // CTA's own barrier; finish_zfill later zeroes those rows of both boxes (whole 128-byte
-          // rows, so the swizzle does not matter) and releases the stage to the leader.
+          // The group's last block ends inside a K step: rows [rem, ceil32(rem)) are not the
+          // group's but are multiplied. It lands on this CTA's own barrier; finish_zfill later
+          // zeroes those rows of both boxes (whole 128-byte rows, so the swizzle does not matter)
+          // and releases the stage to the leader.
           if (lane == 0) {
             mbar_arrive_expect_tx(bar_zfill, STAGE_BYTES);
             tma_load_2d_hint(a_dst, map_a, bar_zfill, xa, y, policy);
@@ -305,6 +311,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           zstage = static_cast<int>(stage);
           zkeep = static_cast<uint32_t>(rem) * 128u;
+          zend = static_cast<uint32_t>((rem + 31) & ~31) * 128u;
         }
         __syncwarp();
         withhold = false;
@@ -350,7 +357,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
         if (t.tokens == 0) continue;
         const int nkb = (t.tokens + TK - 1) / TK;
-        const bool partial = t.tokens % TK != 0;  // the last block was zeroed by generic stores
+        const int rem = t.tokens - TK * (nkb - 1);  // the group's tokens in its last block
+        const int last_steps = (rem + 31) >> 5;     // K steps of the last block
+        const bool zeroed = (rem & 31) != 0;        // its ragged step was zeroed by generic stores
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
@@ -358,7 +367,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                       : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         for (int kb = 0; kb < nkb; ++kb) {
           const uint32_t full = bar_full + 8 * stage;
-          const bool landed = (partial && kb == nkb - 1)
+          const bool landed = (zeroed && kb == nkb - 1)
                                   ? warp_wait<true>(ctl, full, phase, 0x300u | stage)
                                   : warp_wait(ctl, full, phase, 0x300u | stage);
           if (!landed) {
@@ -369,11 +378,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a_stage = base + OFF_RHS + stage * BOX_BYTES;
           const uint32_t b_stage = base + OFF_LHS + stage * BOX_BYTES;
           if (lane == 0) {
+            if (kb < nkb - 1 || last_steps == TK / 32) {
 #pragma unroll
-            for (int ks = 0; ks < TK / 32; ++ks) {
-              const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
-              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
-              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+              for (int ks = 0; ks < TK / 32; ++ks) {
+                const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
+                const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
+                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+              }
+            } else {  // the group's last block: only the steps that hold its tokens
+              for (int ks = 0; ks < last_steps; ++ks) {
+                const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
+                const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
+                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+              }
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
           }

@@ -224,6 +224,13 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
                    static_cast<uint64_t>(slm), box_tokens) != CUDA_SUCCESS ||
       enc_c != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
+  // The pair kernel loads a group's ragged last K step as one 32-token chunk.
+  CUtensorMap map_rhs32, map_lhs32;
+  if (pair && (encode_2d_u8(&map_rhs32, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
+                            static_cast<uint64_t>(srm), 32) != CUDA_SUCCESS ||
+               encode_2d_u8(&map_lhs32, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
+                            static_cast<uint64_t>(slm), 32) != CUDA_SUCCESS))
+    return GGEMM_VARK_ELAYOUT;
 
   vark::TcParams tp;
   tp.group_offs = offs;
@@ -244,7 +251,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   cudaError_t e;
   if (pair) {
     const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;
-    e = vark::tc2_launch(map_lhs, map_rhs, map_c, tp, static_cast<int>(2 * clusters), s);
+    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_c, tp,
+                         static_cast<int>(2 * clusters), s);
   } else {
     const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
     e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);

@@ -92,7 +92,9 @@ cudaError_t tc_set_attributes();
 // col_tiles = ceil(OUT_N / PAIR_COLS), and `grid` must be even (one cluster of two CTAs per pair
 // of SMs).
 size_t tc2_smem_bytes();
+// map_lhs32 / map_rhs32: the same operands with 32-token boxes (a group's ragged last K step).
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
+                       const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
                        const CUtensorMap& map_c, const TcParams& p, int grid,
                        cudaStream_t stream);
 cudaError_t tc2_set_attributes();

@@ -41,15 +41,16 @@
 //
 // Variable K. Loads go through the launch's own tensor maps over all M_total tokens (no map is
 // built on the device). A group's tokens [off_g, off_{g+1}) are walked in blocks of TK aligned
-// to the group's START, so only the last block can hold tokens of other groups (or TMA zero
-// fill past M_total). The MMA warp issues only the K steps (32 tokens) of that block that hold
-// group tokens. When the group ends inside a step, that step's rows past the group must be
-// zero: the block is loaded onto the CTA's own barrier, and at its next stop (after the
-// following stage's empty wait, when the block has usually landed) the producer zeroes those
-// rows in both boxes (both, so that an Inf or NaN in a neighbour's token can never meet a zero
-// and enter the sum as NaN), makes the writes visible to the tensor core (proxy fence) and
-// releases the stage to the leader at cluster scope; the MMA warp waits for such a stage with a
-// cluster-scope acquire. Empty groups skip the pipeline and the epilogue stores zeros.
+// to the group's START. The main ring carries only whole K steps (32 tokens): the last block
+// issues only the steps it holds, and its rows past them are loaded but never multiplied. A
+// group that ends inside a step has a tail of 1..31 tokens. It is loaded at the item's start,
+// one 32-token chunk (second maps with 32-row boxes), into one of two tail buffers per CTA, on
+// the CTA's own barrier. At its next stop the producer zeroes the chunk's rows past the group
+// in both boxes (both, so that an Inf or NaN in a neighbour's token can never meet a zero and
+// enter the sum as NaN), makes the writes visible to the tensor core (proxy fence) and releases
+// the tail to the leader at cluster scope. The MMA warp takes it after the item's whole steps,
+// with a cluster-scope acquire, so the zeroing is off the MMA's critical path. Empty groups
+// skip the pipeline and the epilogue stores zeros.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
 // GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs of the pair, every role leaves its
@@ -79,6 +80,8 @@ constexpr int ST = PAIR_STAGES;
 
 constexpr uint32_t BOX_BYTES = 128 * TK;                 // one operand box per CTA
 constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;          // RHS box + LHS box
+constexpr int SPB = TK / 32;                             // K steps (MMAs) per full stage
+constexpr uint32_t TAIL_BYTES = 128 * 32;                // one operand's 32-token tail chunk
 constexpr uint32_t ACC_COLS = 256;                       // TMEM columns per accumulator
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NACC = 2;
@@ -93,13 +96,14 @@ static_assert(TK % 32 == 0 && TK >= 64 && TK <= 256, "token block: a multiple of
 constexpr uint32_t OFF_RHS = 0;                          // operand A stages
 constexpr uint32_t OFF_LHS = OFF_RHS + ST * BOX_BYTES;   // operand B stages
 constexpr uint32_t OFF_EPI = OFF_LHS + ST * BOX_BYTES;
-constexpr uint32_t OFF_BARS = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1 + 1;
+constexpr uint32_t OFF_TAIL = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;  // 2 x {A, B} tails
+constexpr uint32_t OFF_BARS = OFF_TAIL + 2 * 2 * TAIL_BYTES;
+constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1 + 1 + 2 + 2;
 constexpr uint32_t OFF_MISC = OFF_BARS + NUM_BARS * 8;
 constexpr uint32_t SMEM_USED = OFF_MISC + 16;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
-static_assert(OFF_EPI % 1024 == 0, "alignment");
+static_assert(OFF_EPI % 1024 == 0 && OFF_TAIL % 1024 == 0, "alignment");
 
 // Instruction descriptors without N: the item's N is or-ed in at run time.
 constexpr uint32_t IDESC_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
@@ -180,6 +184,8 @@ __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool re
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     vark_tc2_kernel(const __grid_constant__ CUtensorMap map_lhs,
                     const __grid_constant__ CUtensorMap map_rhs,
+                    const __grid_constant__ CUtensorMap map_lhs32,
+                    const __grid_constant__ CUtensorMap map_rhs32,
                     const __grid_constant__ CUtensorMap map_c, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -196,7 +202,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t bar_tfull = bar_empty + 8 * ST;     // [2]   both CTAs
   const uint32_t bar_tempty = bar_tfull + 16;        // [2]   used in the leader only
   const uint32_t bar_drain = bar_tempty + 16;        // [1]   leader
-  const uint32_t bar_zfill = bar_drain + 8;          // [1]   both CTAs: a group's last block
+  const uint32_t bar_zfill = bar_drain + 8;          // [1]   both CTAs: a tail's own loads
+  const uint32_t bar_tail_full = bar_zfill + 8;      // [2]   leader: both tails zeroed
+  const uint32_t bar_tail_empty = bar_tail_full + 16;  // [2] both CTAs: the leader's commit
   uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(sbase + OFF_MISC + 4);
 
@@ -213,9 +221,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(bar_drain, 1);
     mbar_init(bar_zfill, 1);  // this CTA's producer
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_tail_full + 8 * i, 2);   // each CTA's producer, after zeroing
+      mbar_init(bar_tail_empty + 8 * i, 1);  // the leader's commit
+    }
     fence_mbar_init();
     tma_prefetch_desc(&map_lhs);
     tma_prefetch_desc(&map_rhs);
+    tma_prefetch_desc(&map_lhs32);
+    tma_prefetch_desc(&map_rhs32);
     tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
@@ -240,24 +254,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     bool withhold =
         p.status != nullptr && *reinterpret_cast<volatile uint32_t*>(p.status + 3) ==
                                    GGEMM_VARK_TEST_STALL_MAGIC;
-    uint32_t stage = 0, phase = 0, zphase = 0;
+    uint32_t stage = 0, phase = 0, zphase = 0, ntail = 0;
     bool ok = true;
-    // A group's last block whose rows past the group still have to be zeroed (-1: none). Its
-    // zeroing is finished at the producer's next stop, after the following stage's empty wait:
-    // by then the block has usually landed, and the MMA warp still has the stages before it.
-    int zstage = -1;
-    uint32_t zkeep = 0, zend = 0;
+    // A tail whose rows past the group still have to be zeroed (-1: none). The zeroing is
+    // finished at the producer's next stop, when the tail has usually landed; the MMA warp only
+    // needs the tail after the item's whole K steps.
+    int ztail = -1;
+    uint32_t zkeep = 0;
     auto finish_zfill = [&]() -> bool {
-      if (zstage < 0) return true;
+      if (ztail < 0) return true;
       if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) return false;
       zphase ^= 1u;
-      const uint32_t zs = static_cast<uint32_t>(zstage);
-      smem_zero_warp(base + OFF_RHS + zs * BOX_BYTES + zkeep, zend - zkeep, lane);
-      smem_zero_warp(base + OFF_LHS + zs * BOX_BYTES + zkeep, zend - zkeep, lane);
+      const uint32_t ta = base + OFF_TAIL + static_cast<uint32_t>(ztail) * 2u * TAIL_BYTES;
+      smem_zero_warp(ta + zkeep, TAIL_BYTES - zkeep, lane);
+      smem_zero_warp(ta + TAIL_BYTES + zkeep, TAIL_BYTES - zkeep, lane);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive_release_cluster(mapa_shared(bar_full + 8 * zs, 0));
-      zstage = -1;
+      if (lane == 0) mbar_arrive_release_cluster(mapa_shared(bar_tail_full + 8 * ztail, 0));
+      ztail = -1;
       return true;
     };
     Item nxt = decode_item(p, cluster, false);
@@ -265,8 +279,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const Item t = nxt;  // decoded one item ahead: the offsets' load latency is hidden
       if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
       if (t.tokens == 0) continue;
-      const int nkb = (t.tokens + TK - 1) / TK;
-      const int rem = t.tokens - TK * (nkb - 1);  // the group's tokens in its last block
+      const int steps = t.tokens >> 5;                 // whole 32-token K steps
+      const int ragged = t.tokens & 31;                // tokens of the tail step
+      const int nkb = (steps + SPB - 1) / SPB;         // main-ring blocks
       // First token of the group as a TMA row coordinate (token_limit <= INT32_MAX).
       const int32_t lo = static_cast<int32_t>(t.end - t.tokens);
       // A: this CTA's 128 C columns (RHS); B: this CTA's half of the item's rows (LHS). Edge
@@ -275,43 +290,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int32_t r = static_cast<int32_t>(rank);
       const int32_t xa = t.edge ? t.m0 + PAIR_HALF * r : t.n0 + PAIR_HALF * r;
       const int32_t xb = t.edge ? t.n0 + (t.ecols >> 1) * r : t.m0 + (t.nrows >> 1) * r;
+      if (ragged != 0) {
+        // The tail: one 32-token chunk from the group's last whole step on, into a tail buffer
+        // (two, used in turn), loaded first so that its zeroing is long done when the MMA warp
+        // reaches it. Rows [ragged, 32) of it are not the group's (another group's tokens, or
+        // TMA zero fill past M_total).
+        const uint32_t tb = ntail & 1u;
+        const uint32_t tpar = ((ntail >> 1) & 1u) ^ 1u;
+        if (!finish_zfill() || !warp_wait(ctl, bar_tail_empty + 8 * tb, tpar, 0x700u | tb)) {
+          ok = false;
+          break;
+        }
+        ++ntail;
+        const uint32_t ta = base + OFF_TAIL + tb * 2u * TAIL_BYTES;
+        const int32_t y = lo + 32 * steps;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar_zfill, 2u * TAIL_BYTES);
+          tma_load_2d_hint(ta, t.edge ? &map_lhs32 : &map_rhs32, bar_zfill, xa, y, policy);
+          tma_load_2d_hint(ta + TAIL_BYTES, t.edge ? &map_rhs32 : &map_lhs32, bar_zfill, xb, y,
+                           policy);
+        }
+        ztail = static_cast<int>(tb);
+        zkeep = static_cast<uint32_t>(ragged) * 128u;
+      }
       const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
       const CUtensorMap* const map_b = t.edge ? &map_rhs : &map_lhs;
       for (int kb = 0; kb < nkb; ++kb) {
-        // The empty wait does not depend on a pending last block: this stage's previous fill
-        // is ST - 1 stages older than that block in the MMA warp's order.
+        // Neither wait depends on the pending tail: the MMA warp takes it after the item's
+        // whole steps, and this stage's previous fill is older than all of them.
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage) ||
             !finish_zfill()) {
           ok = false;
           break;
         }
-        const uint32_t a_dst = base + OFF_RHS + stage * BOX_BYTES;
-        const uint32_t b_dst = base + OFF_LHS + stage * BOX_BYTES;
-        const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
-        const int32_t y = lo + TK * kb;
-        if (withhold) {
-          // nothing issued: the leader's wait on this stage runs out
-        } else if (kb < nkb - 1 || (rem & 31) == 0) {
-          // (a last block that ends on a 32-token step: the MMA warp issues only rem / 32 steps,
-          // so the rows past the group are never multiplied)
-          if (lane == 0) {
-            mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
-            tma_load_2d_pair(a_dst, map_a, fb, xa, y, policy);
-            tma_load_2d_pair(b_dst, map_b, fb, xb, y, policy);
-          }
-        } else {
-          // The group's last block ends inside a K step: rows [rem, ceil32(rem)) are not the
-          // group's but are multiplied. It lands on this CTA's own barrier; finish_zfill later
-          // zeroes those rows of both boxes (whole 128-byte rows, so the swizzle does not matter)
-          // and releases the stage to the leader.
-          if (lane == 0) {
-            mbar_arrive_expect_tx(bar_zfill, STAGE_BYTES);
-            tma_load_2d_hint(a_dst, map_a, bar_zfill, xa, y, policy);
-            tma_load_2d_hint(b_dst, map_b, bar_zfill, xb, y, policy);
-          }
-          zstage = static_cast<int>(stage);
-          zkeep = static_cast<uint32_t>(rem) * 128u;
-          zend = static_cast<uint32_t>((rem + 31) & ~31) * 128u;
+        if (lane == 0 && !withhold) {
+          // The last block's rows past the whole steps are loaded but never multiplied.
+          const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
+          const int32_t y = lo + TK * kb;
+          mbar_arrive_expect_tx_cluster(fb, STAGE_BYTES);
+          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, map_a, fb, xa, y, policy);
+          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, map_b, fb, xb, y, policy);
         }
         __syncwarp();
         withhold = false;
@@ -322,11 +340,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (ok && !finish_zfill()) ok = false;
-    // Loads still in flight are drained through the empty barriers: every stage this producer
-    // filled is released by the leader's commit once its MMAs (which waited for the data)
-    // finish; a last block still pending after an abort is drained on its own barrier. After an
+    // Loads still in flight are drained through the empty barriers: every stage and tail this
+    // producer filled is released by the leader's commit once its MMAs (which waited for the
+    // data) finish; a tail still pending after an abort is drained on its own barrier. After an
     // abort the waits are bounded.
-    const bool zpending = zstage >= 0;
     if (lane == 0) {
       for (int s = 0; s < ST; ++s) {
         const uint64_t t0 = globaltimer_ns();
@@ -337,7 +354,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
         }
       }
-      if (zpending) {
+      for (uint32_t tb = 0; tb < 2; ++tb) {
+        const uint32_t uses = (ntail + 1u - tb) >> 1;  // tail buffer tb holds uses 0, 2, 4 ... or 1, 3 ...
+        if (uses == 0) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_tail_empty + 8 * tb, (uses - 1u) & 1u)) {
+          if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
+        }
+      }
+      if (ztail >= 0) {
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(bar_zfill, zphase)) {
           if (globaltimer_ns() - t0 > ctl.timeout_ns) break;
@@ -348,7 +373,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer (pair leader only) ==================================
     if (leader) {
-      uint32_t stage = 0, phase = 0;
+      uint32_t stage = 0, phase = 0, ntail = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
       Item nxt = decode_item(p, cluster, false);
@@ -356,21 +381,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const Item t = nxt;
         if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
         if (t.tokens == 0) continue;
-        const int nkb = (t.tokens + TK - 1) / TK;
-        const int rem = t.tokens - TK * (nkb - 1);  // the group's tokens in its last block
-        const int last_steps = (rem + 31) >> 5;     // K steps of the last block
-        const bool zeroed = (rem & 31) != 0;        // its ragged step was zeroed by generic stores
+        const int steps = t.tokens >> 5;
+        const int ragged = t.tokens & 31;
+        const int nkb = (steps + SPB - 1) / SPB;
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
         const uint32_t idesc = t.edge ? IDESC_EDGE_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
                                       : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         for (int kb = 0; kb < nkb; ++kb) {
-          const uint32_t full = bar_full + 8 * stage;
-          const bool landed = (zeroed && kb == nkb - 1)
-                                  ? warp_wait<true>(ctl, full, phase, 0x300u | stage)
-                                  : warp_wait(ctl, full, phase, 0x300u | stage);
-          if (!landed) {
+          if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
             ok = false;
             break;
           }
@@ -378,15 +398,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a_stage = base + OFF_RHS + stage * BOX_BYTES;
           const uint32_t b_stage = base + OFF_LHS + stage * BOX_BYTES;
           if (lane == 0) {
-            if (kb < nkb - 1 || last_steps == TK / 32) {
+            const int ks_n = kb < nkb - 1 ? SPB : steps - SPB * (nkb - 1);
+            if (ks_n == SPB) {
 #pragma unroll
-              for (int ks = 0; ks < TK / 32; ++ks) {
+              for (int ks = 0; ks < SPB; ++ks) {
                 const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
                 const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
                 mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
               }
-            } else {  // the group's last block: only the steps that hold its tokens
-              for (int ks = 0; ks < last_steps; ++ks) {
+            } else {  // the last block: only its whole steps
+              for (int ks = 0; ks < ks_n; ++ks) {
                 const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
                 const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
                 mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
@@ -401,6 +422,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
         }
         if (!ok) break;
+        if (ragged != 0) {
+          // The tail step: its rows past the group were zeroed by both producers (generic
+          // stores released at cluster scope).
+          const uint32_t tb = ntail & 1u;
+          const uint32_t tpar = (ntail >> 1) & 1u;
+          ++ntail;
+          if (!warp_wait<true>(ctl, bar_tail_full + 8 * tb, tpar, 0x800u | tb)) break;
+          tc_fence_after_sync();
+          if (lane == 0) {
+            const uint32_t ta = base + OFF_TAIL + tb * 2u * TAIL_BYTES;
+            mma_f8f6f4_pair(d_tmem, smem_desc_sw128(ta, TAIL_BYTES, 1024u),
+                            smem_desc_sw128(ta + TAIL_BYTES, TAIL_BYTES, 1024u), idesc,
+                            steps > 0 ? 1u : 0u);
+            mma_commit_pair(bar_tail_empty + 8 * tb, 0x3);  // frees the tail in both CTAs
+          }
+          __syncwarp();
+        }
         if (lane == 0) mma_commit_pair(bar_tfull + 8 * acc, 0x3);  // accumulator ready
         __syncwarp();
         if (++acc == NACC) {
@@ -585,9 +623,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 size_t tc2_smem_bytes() { return SMEM_ALLOC; }
 
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
+                       const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
                        const CUtensorMap& map_c, const TcParams& p, int grid,
                        cudaStream_t stream) {
-  vark_tc2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_lhs, map_rhs, map_c, p);
+  vark_tc2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(map_lhs, map_rhs, map_lhs32,
+                                                              map_rhs32, map_c, p);
   return cudaGetLastError();
 }
 

@@ -63,6 +63,10 @@ RAGGED = [
     [300, 0, 77, 160, 487],
     [0, 0, 0],
     [4096],
+    # hundreds of groups, so each CTA pair works through many items: every item below 32 tokens
+    # is only a ragged tail step, and the tail buffers are reused item after item
+    [7] * 300,
+    [(i * 37) % 101 for i in range(240)],  # tails only, whole steps only, and mixed
 ]
 
 

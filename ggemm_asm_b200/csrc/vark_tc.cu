@@ -23,12 +23,12 @@
 // Variable K. A group's tokens [off_g, off_{g+1}) are walked in blocks of 128 that are aligned
 // to the START of the group, through the launch's own tensor maps over all M_total tokens (no
 // map is built on the device). Only the last block can hold rows that are not the group's
-// (another group's tokens, or TMA zero fill past M_total). That block completes on a second
-// barrier; the producer zeroes those rows in every box of the stage (all operands, so that a
-// neighbour's Inf or NaN never meets a zero and enters the sum as NaN), makes the writes visible
-// to the tensor core (proxy fence) and then releases the stage to the MMA warp. Every stage is
-// a uniform 4 MMAs (stages with fewer MMAs stall the recycled-stage pipeline on this hardware).
-// Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
+// (another group's tokens, or TMA zero fill past M_total); the MMA warp issues only its K steps
+// (32 tokens) that hold group tokens. When the group ends inside a step, that block completes on
+// a second barrier; the producer zeroes the step's rows past the group in every box of the stage
+// (all operands, so that a neighbour's Inf or NaN never meets a zero and enters the sum as NaN),
+// makes the writes visible to the tensor core (proxy fence) and then releases the stage to the
+// MMA warp. Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
 //
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA sets the abort
 // flag and GGEMM_VARK_DEV_TIMEOUT in the status block, every role leaves its loop, in-flight
@@ -218,10 +218,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t rhs_dst = base + OFF_RHS + stage * RHS_STAGE_BYTES;
         const uint32_t lhs_dst = base + OFF_LHS + stage * LHS_STAGE_BYTES;
         const int32_t y = lo + TILE_TOKENS * kb;
-        const bool last_partial = kb == nkb - 1 && rem < TILE_TOKENS;
+        // A group's last block that ends inside a K step (32 tokens): the MMA warp multiplies
+        // that step, so its rows [rem, ceil32(rem)) must be zero. The block lands on bar_zfill
+        // instead and those rows are zeroed before the stage is released to the MMA warp. (The
+        // MMA warp issues only the steps that hold group tokens, so a block ending on a step
+        // boundary needs nothing.)
+        const bool last_partial = kb == nkb - 1 && (rem & 31) != 0;
         if (!withhold) {
-          // A group's last, partial block lands on bar_zfill instead: its rows [rem, 128) are
-          // zeroed before the stage is released to the MMA warp.
           const uint32_t lb = last_partial ? bar_zfill : fb;
           if (lane == 0) {
             mbar_arrive_expect_tx(lb, STAGE_TX_BYTES);
@@ -241,10 +244,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             zphase ^= 1u;
             // Whole 128-byte token rows, so the 128-byte swizzle does not matter.
             const uint32_t keep = static_cast<uint32_t>(rem) * 128u;
-            smem_zero_warp(rhs_dst + keep, RHS_STAGE_BYTES - keep, lane);
+            const uint32_t zbytes = static_cast<uint32_t>((rem + 31) & ~31) * 128u - keep;
+            smem_zero_warp(rhs_dst + keep, zbytes, lane);
 #pragma unroll
             for (int b = 0; b < LHS_BOXES; ++b)
-              smem_zero_warp(lhs_dst + b * LHS_BOX_BYTES + keep, LHS_BOX_BYTES - keep, lane);
+              smem_zero_warp(lhs_dst + b * LHS_BOX_BYTES + keep, zbytes, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(fb);
@@ -288,6 +292,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const TileInfo t = decode_tile(p, tile, false);
       if (t.tokens == 0) continue;
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
+      const int last_steps = (t.tokens - TILE_TOKENS * (nkb - 1) + 31) >> 5;  // of the last block
       if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
       tc_fence_after_sync();
       const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE_COLS;
@@ -300,11 +305,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t a_stage = base + OFF_RHS + stage * RHS_STAGE_BYTES;
         const uint32_t b_stage = base + OFF_LHS + stage * LHS_STAGE_BYTES;
         if (lane == 0) {
+          if (kb < nkb - 1 || last_steps == TILE_TOKENS / 32) {
 #pragma unroll
-          for (int ks = 0; ks < TILE_TOKENS / 32; ++ks) {
-            const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, RHS_STAGE_BYTES, 1024u);
-            const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, LHS_BOX_BYTES, 1024u);
-            mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+            for (int ks = 0; ks < TILE_TOKENS / 32; ++ks) {
+              const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, RHS_STAGE_BYTES, 1024u);
+              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, LHS_BOX_BYTES, 1024u);
+              mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+            }
+          } else {  // the group's last block: only the K steps that hold its tokens
+            for (int ks = 0; ks < last_steps; ++ks) {
+              const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, RHS_STAGE_BYTES, 1024u);
+              const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, LHS_BOX_BYTES, 1024u);
+              mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+            }
           }
           mma_commit(bar_empty + 8 * stage);  // frees the stage once these MMAs finish
         }

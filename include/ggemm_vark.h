@@ -80,8 +80,8 @@ extern "C" {
  * the reference's (README.md:88-95). Per-tensor scales (one fp32 each). The token count
  * M_total is not an argument, exactly as in the reference: group_offs is trusted to lie inside
  * the LHS/RHS allocations. The first call on a device makes the library's one allocation for
- * that device (cudaMalloc, about 0.5 MiB: the status block and a per-SM ring of tensor maps
- * that the kernel builds for each group); make the first call before any stream capture.
+ * that device (cudaMalloc of the 4 KiB status block); make the first call before any stream
+ * capture.
  */
 GGEMM_VARK_API int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* c,
                          const float* lhs_scale, const float* rhs_scale,

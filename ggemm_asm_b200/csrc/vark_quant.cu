@@ -43,12 +43,28 @@ constexpr int kThreads = 512;  // threads doing the arithmetic (register-load ke
 constexpr int kUnroll = 4;
 constexpr int kWarps = kThreads / 32;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
-// Bulk-copy kernel: kThreads consumer threads plus one producer warp, and a ring of QT_STAGES
-// chunks of QT_CHUNK bytes (32 KB x 3 measured faster than 16 KB x 6 and 8 KB x 12: fewer
-// hand-offs per byte; two CTAs fit on an SM).
-constexpr int kTmaThreads = kThreads + 32;
-constexpr uint32_t QT_CHUNK = 32768;
-constexpr int QT_STAGES = 3;
+// Bulk-copy kernel: kQtThreads consumer threads plus one producer warp, and a ring of QT_STAGES
+// chunks of at most QT_CHUNK bytes, one CTA per SM. 64 KB x 3 measured fastest at the gate_up
+// shapes: against 32 KB x 3 with two CTAs per SM it takes 11% less time on x [131072, 2880], 13%
+// less on dy [131072, 5760] and 8% less on dy under skewed routing (half as many CTAs meet in
+// each unit's grid-wide wait, and fewer hand-offs per byte); 48 KB x 4, 56 or 72 KB x 3 and
+// 1024 consumer threads were slower, and 96 KB x 2 was faster on x alone but 9% slower on dy.
+#ifndef VARK_QT_CONSUMERS
+#define VARK_QT_CONSUMERS 512
+#endif
+constexpr int kQtThreads = VARK_QT_CONSUMERS;  // consumer threads of the bulk-copy kernel
+constexpr int kQtWarps = kQtThreads / 32;
+static_assert(kQtThreads % 32 == 0 && kQtThreads + 32 <= 1024, "bulk-copy kernel block size");
+constexpr int kTmaThreads = kQtThreads + 32;
+#ifndef VARK_QT_CHUNK
+#define VARK_QT_CHUNK 65536
+#endif
+#ifndef VARK_QT_STAGES
+#define VARK_QT_STAGES 3
+#endif
+constexpr uint32_t QT_CHUNK = VARK_QT_CHUNK;
+static_assert(QT_CHUNK % 16 == 0, "chunk: whole 16-byte vectors");
+constexpr int QT_STAGES = VARK_QT_STAGES;
 constexpr size_t QT_SMEM = static_cast<size_t>(QT_STAGES) * QT_CHUNK + 2 * QT_STAGES * 8 + 128;
 
 struct QuantParams {
@@ -396,25 +412,48 @@ __global__ void __launch_bounds__(kThreads) vark_quant_kernel(const QuantParams 
 
 // Order of the chunks within a stage: the amax reads of unit s run QT_LEAD chunks ahead of the
 // quantise reads of unit s-1, so the wait for unit s-1's scale overlaps real work (it costs
-// QT_LEAD chunks per CTA of extra L2 footprint, ~19 MB over the grid at 32 KB x 2).
-constexpr int64_t QT_LEAD = 2;
+// QT_LEAD chunks per CTA of extra L2 footprint, ~19 MB over 148 CTAs at 64 KB x 2). The quantise
+// pass takes a unit's chunks oldest first; newest first measured 4-11% slower.
+#ifndef VARK_QT_LEAD
+#define VARK_QT_LEAD 2
+#endif
+constexpr int64_t QT_LEAD = VARK_QT_LEAD;
 __device__ __forceinline__ bool amax_next(int64_t ta, int64_t tb, int64_t na, int64_t nb) {
   return ta < na && (tb == nb || ta < tb + QT_LEAD);
 }
 
-// This CTA's slice of unit w: byte range [b0, b1) and whether the unit is valid and non-empty.
+// This CTA's slice of unit w: byte range [b0, b1), whether the unit is valid and non-empty, and
+// its cut into n chunks of cb bytes (the last one shorter). The chunks are as equal as 16-byte
+// granularity allows: a short last chunk would hold a whole ring stage for few bytes in flight.
 struct Slice {
   int64_t b0, b1;
   bool unit_ok;
-  __device__ __forceinline__ int64_t chunks() const { return (b1 - b0 + QT_CHUNK - 1) / QT_CHUNK; }
+  int64_t n;
+  uint32_t cb;
+  __device__ __forceinline__ int64_t chunks() const { return n; }
+  __device__ __forceinline__ int64_t chunk_offset(int64_t t) const { return t * cb; }
   __device__ __forceinline__ uint32_t chunk_bytes(int64_t t) const {
-    const int64_t rest = b1 - b0 - t * QT_CHUNK;
-    return static_cast<uint32_t>(rest < QT_CHUNK ? rest : QT_CHUNK);
+    const int64_t rest = b1 - b0 - t * cb;
+    return static_cast<uint32_t>(rest < cb ? rest : cb);
   }
 };
 
+// Equal chunks of at most QT_CHUNK bytes over len bytes (len a multiple of 16).
+__device__ __forceinline__ void cut_slice(Slice& sl) {
+  const int64_t len = sl.b1 - sl.b0;
+  if (len <= 0) {
+    sl.n = 0;
+    sl.cb = QT_CHUNK;
+    return;
+  }
+  const int64_t n0 = (len + QT_CHUNK - 1) / QT_CHUNK;
+  const int64_t cb = ((len + n0 - 1) / n0 + 15) / 16 * 16;  // <= QT_CHUNK (a multiple of 16)
+  sl.cb = static_cast<uint32_t>(cb);
+  sl.n = (len + cb - 1) / cb;  // every chunk non-empty
+}
+
 __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
-  Slice sl{0, 0, false};
+  Slice sl{0, 0, false, 0, QT_CHUNK};
   if (w < 0 || w >= p.units) return sl;
   int64_t lo, hi;
   if (!unit_rows(p, w, &lo, &hi) || hi == lo) return sl;
@@ -424,6 +463,7 @@ __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
   sl.b0 = lo * p.stride_x + v0 * 16;
   sl.b1 = lo * p.stride_x + v1 * 16;
   sl.unit_ok = true;
+  cut_slice(sl);
   return sl;
 }
 
@@ -436,7 +476,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, uint64_t
   return true;
 }
 
-// Barrier 1 joins the kThreads consumer threads only (the producer warp never takes part).
+// Barrier 1 joins the kQtThreads consumer threads only (the producer warp never takes part).
 __device__ __forceinline__ bool consumers_sync_or(bool v) {
   uint32_t r;
   asm volatile(
@@ -445,13 +485,13 @@ __device__ __forceinline__ bool consumers_sync_or(bool v) {
       "bar.red.or.pred q, 1, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(kThreads)
+      : "r"(static_cast<uint32_t>(v)), "n"(kQtThreads)
       : "memory");
   return r != 0;
 }
 
 __device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(kQtThreads) : "memory");
 }
 
 // Producer warp, lane 0: issue every chunk in the consumers' order once its stage is free;
@@ -478,7 +518,7 @@ struct Producer {
     const uint32_t bytes = sl.chunk_bytes(t);
     const uint32_t bar = smem_u32(full + k);
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_load_1d(stage0 + k * QT_CHUNK, p.x + sl.b0 + t * QT_CHUNK, bytes, bar,
+    bulk_load_1d(stage0 + k * QT_CHUNK, p.x + sl.b0 + sl.chunk_offset(t), bytes, bar,
                  first_read ? pol_keep : pol_last);
     ++n;
   }
@@ -502,14 +542,14 @@ struct Producer {
   }
 };
 
-// Consumer warps (kThreads threads): the same chunk order as the producer.
+// Consumer warps (kQtThreads threads): the same chunk order as the producer.
 template <bool E5M2>
 struct Consumer {
   const QuantParams& p;
   uint8_t* stages;
   uint64_t* full;
   uint64_t* empty;
-  uint32_t* red;       // kWarps words
+  uint32_t* red;       // kQtWarps words
   int lane, warp;
   int64_t j = 0;       // chunks consumed
   bool fail = false;
@@ -542,7 +582,7 @@ struct Consumer {
       return;
     }
     const uint32_t nv = sl.chunk_bytes(t) / 16;
-    for (uint32_t v = threadIdx.x; v < nv; v += kThreads) {
+    for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads) {
       const uint4 x = st[v];
       m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
       m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
@@ -561,12 +601,12 @@ struct Consumer {
     }
     const uint32_t nv = sl.chunk_bytes(t) / 16;
     // contiguous rows: element index = byte offset / 2
-    uint2* dst = reinterpret_cast<uint2*>(p.q + (sl.b0 + t * QT_CHUNK) / 2);
+    uint2* dst = reinterpret_cast<uint2*>(p.q + (sl.b0 + sl.chunk_offset(t)) / 2);
     if (fast) {
-      for (uint32_t v = threadIdx.x; v < nv; v += kThreads)
+      for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads)
         __stcs(dst + v, quant_vec<E5M2, true>(st[v], scale, recip));
     } else {
-      for (uint32_t v = threadIdx.x; v < nv; v += kThreads)
+      for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads)
         __stcs(dst + v, quant_vec<E5M2, false>(st[v], scale, recip));
     }
     release(k);
@@ -581,7 +621,7 @@ struct Consumer {
     uint32_t mm = 0;
     if (threadIdx.x == 0) {
 #pragma unroll
-      for (int k = 0; k < kWarps; ++k) mm = max(mm, red[k]);
+      for (int k = 0; k < kQtWarps; ++k) mm = max(mm, red[k]);
     }
     consumers_sync();  // red[] may be rewritten after this
     if (threadIdx.x == 0) {  // the atomics and their fence hold up thread 0 only
@@ -649,18 +689,18 @@ __global__ void __launch_bounds__(kTmaThreads) vark_quant_tma_kernel(const Quant
                                              ~static_cast<uintptr_t>(127));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + QT_STAGES * QT_CHUNK);
   uint64_t* empty = full + QT_STAGES;
-  __shared__ uint32_t red[kWarps];
+  __shared__ uint32_t red[kQtWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int k = 0; k < QT_STAGES; ++k) {
       mbar_init(smem_u32(full + k), 1);
-      mbar_init(smem_u32(empty + k), kWarps);
+      mbar_init(smem_u32(empty + k), kQtWarps);
     }
     fence_mbar_init();
   }
   __syncthreads();  // the only barrier with the producer warp
-  if (warp == kWarps) {
+  if (warp == kQtWarps) {
     if (lane == 0) {
       Producer pr{p, smem_u32(smem), full, empty, l2_policy_evict_last(),
                   l2_policy_evict_first()};

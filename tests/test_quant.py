@@ -319,6 +319,30 @@ def test_quantize_full_size_gate_up(fmt, F):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("granularity", ["group", "tensor"])
+def test_quantize_long_slices(granularity):
+    """Units of 50-130 MB: each CTA's slice is cut into many equal bulk-copy chunks whose sizes
+    are not a power of two (rows of 2000 bytes, slices of odd vector counts). Every unit against
+    the quotient formula evaluated with torch on the device."""
+    lens = [40000, 3, 25001]
+    F = 1000
+    offs = torch.from_numpy(inputs.offsets_from_lens(lens))
+    g = torch.Generator(device="cuda").manual_seed(77)
+    x = (torch.randn(sum(lens), F, generator=g, device="cuda") * 3.0).to(torch.bfloat16)
+    q, s = quantize_fp8(x, offs.cuda(), "e4m3", granularity=granularity)
+    torch.cuda.synchronize()
+    dtype, fmax = vo.FP8_FORMATS["e4m3"]
+    fm = torch.tensor(fmax, device="cuda")
+    units = [(0, len(lens))] if granularity == "tensor" else [(e, e + 1) for e in range(len(lens))]
+    for u, (a, b) in enumerate(units):
+        lo, hi = int(offs[a]), int(offs[b])
+        su = x[lo:hi].float().abs().amax() / fm
+        assert torch.equal(s[u], su)
+        ref = (x[lo:hi].float() / su).clamp(-fmax, fmax).to(dtype)
+        assert torch.equal(q[lo:hi].view(torch.uint8), ref.view(torch.uint8)), u
+
+
+@pytest.mark.gpu
 def test_quantize_expired_wait_is_reported():
     """Test hook: CTA 0 withholds its first arrival, so every CTA's wait expires; the call stops
     by itself, reports GGEMM_VARK_DEV_TIMEOUT, and the next call is correct."""

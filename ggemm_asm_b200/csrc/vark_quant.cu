@@ -17,9 +17,10 @@
 //  - A CTA reduces the amax of its slice of unit u, publishes it (one atomicMax on the unit's
 //    word, then an arrival count), waits until every CTA has published, and quantises the same
 //    slice. All CTAs hold equal shares of a unit, so the wait is short.
-//  - The second read of a row comes from L2: the distance between the two reads is one unit (up
-//    to ~47 MB at 4096 x 5760 bf16), which B200's 126 MB L2 holds, so HBM sees each element read
-//    once (measured: DRAM reads equal to the input size).
+//  - The second read of a row mostly comes from L2: the distance between the two reads is about
+//    one unit (up to ~47 MB at 4096 x 5760 bf16) and B200's L2 is 126 MB. Measured DRAM reads:
+//    exactly the input size when a unit's quantise pass directly follows its amax pass, 1.23x
+//    the input with the interleaved order below (which keeps HBM reading while stores drain).
 //  - Contiguous rows (the usual layout): one producer warp streams the CTA's slices through a
 //    ring of shared-memory chunks with 1-D bulk copies (cp.async.bulk), running ahead across the
 //    amax/quantise boundary; the 16 consumer warps release chunks through mbarriers and meet at

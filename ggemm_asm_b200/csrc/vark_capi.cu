@@ -120,13 +120,14 @@ int check_args(const void* lhs, const void* rhs, void* c, const float* ls, const
 }
 
 CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                      uint64_t row_pitch, uint32_t box_tokens) {
+                      uint64_t row_pitch, uint32_t box_tokens, uint32_t box_inner = 128,
+                      CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_pitch};
-  const cuuint32_t box[2] = {128, box_tokens};
+  const cuuint32_t box[2] = {box_inner, box_tokens};
   const cuuint32_t estr[2] = {1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -224,12 +225,20 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
                    static_cast<uint64_t>(slm), box_tokens) != CUDA_SUCCESS ||
       enc_c != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
-  // The pair kernel loads a group's ragged last K step as one 32-token chunk.
-  CUtensorMap map_rhs32, map_lhs32;
+  // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the LHS of
+  // items with at most 64 C rows through narrow boxes.
+  CUtensorMap map_rhs32, map_lhs32, map_lhs_n, map_lhs32_n;
+  const uint32_t nw = static_cast<uint32_t>(vark::PAIR_NARROW_W);
   if (pair && (encode_2d_u8(&map_rhs32, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
                             static_cast<uint64_t>(srm), 32) != CUDA_SUCCESS ||
                encode_2d_u8(&map_lhs32, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                            static_cast<uint64_t>(slm), 32) != CUDA_SUCCESS))
+                            static_cast<uint64_t>(slm), 32) != CUDA_SUCCESS ||
+               encode_2d_u8(&map_lhs_n, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
+                            static_cast<uint64_t>(slm), box_tokens, nw,
+                            CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
+               encode_2d_u8(&map_lhs32_n, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
+                            static_cast<uint64_t>(slm), 32, nw,
+                            CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS))
     return GGEMM_VARK_ELAYOUT;
 
   vark::TcParams tp;
@@ -251,8 +260,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   cudaError_t e;
   if (pair) {
     const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;
-    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_c, tp,
-                         static_cast<int>(2 * clusters), s);
+    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c,
+                         tp, static_cast<int>(2 * clusters), s);
   } else {
     const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
     e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);

@@ -92,9 +92,14 @@ cudaError_t tc_set_attributes();
 // col_tiles = ceil(OUT_N / PAIR_COLS), and `grid` must be even (one cluster of two CTAs per pair
 // of SMs).
 size_t tc2_smem_bytes();
+// map_lhs / map_rhs: 2-D u8 {features, tokens}, box {128, PAIR_TOKENS}, 128-byte swizzle.
 // map_lhs32 / map_rhs32: the same operands with 32-token boxes (a group's ragged last K step).
+// map_lhs_n / map_lhs32_n: LHS with boxes {PAIR_NARROW_W, PAIR_TOKENS} and {PAIR_NARROW_W, 32},
+// 32-byte swizzle, for items whose MMA N is at most 2 * PAIR_NARROW_W.
+constexpr int PAIR_NARROW_W = 32;
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
+                       const CUtensorMap& map_lhs_n, const CUtensorMap& map_lhs32_n,
                        const CUtensorMap& map_c, const TcParams& p, int grid,
                        cudaStream_t stream);
 cudaError_t tc2_set_attributes();

@@ -94,13 +94,15 @@ int setup(Device** out) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 CUresult encode_operand(CUtensorMap* m, const void* base, int32_t features, uint64_t tokens,
-                        int32_t pitch, uint32_t box_tokens = vark::PAIR_TOKENS) {
+                        int32_t pitch, uint32_t box_tokens = vark::PAIR_TOKENS,
+                        uint32_t box_inner = 128,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(features), tokens};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[2] = {128, box_tokens};
+  const cuuint32_t box[2] = {box_inner, box_tokens};
   const cuuint32_t estr[2] = {1, 1};
   return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -156,11 +158,16 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   const int64_t token_limit =
       m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
   const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
-  CUtensorMap map_lhs, map_rhs, map_lhs32, map_rhs32, map_c;
+  CUtensorMap map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c;
+  const uint32_t nw = static_cast<uint32_t>(vark::PAIR_NARROW_W);
   if (encode_operand(&map_lhs, lhs, OUT_M, token_dim, stride_lhs_m) != CUDA_SUCCESS ||
       encode_operand(&map_rhs, rhs, OUT_N, token_dim, stride_rhs_m) != CUDA_SUCCESS ||
       encode_operand(&map_lhs32, lhs, OUT_M, token_dim, stride_lhs_m, 32) != CUDA_SUCCESS ||
       encode_operand(&map_rhs32, rhs, OUT_N, token_dim, stride_rhs_m, 32) != CUDA_SUCCESS ||
+      encode_operand(&map_lhs_n, lhs, OUT_M, token_dim, stride_lhs_m, vark::PAIR_TOKENS, nw,
+                     CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
+      encode_operand(&map_lhs32_n, lhs, OUT_M, token_dim, stride_lhs_m, 32, nw,
+                     CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
       encode_out(&map_c, c, G, OUT_M, OUT_N, stride_cg, stride_cm) != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
 
@@ -190,8 +197,8 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   tp.stride_cm = stride_cm;
   const int64_t clusters = items < d->sm_count / 2 ? items : d->sm_count / 2;
   const cudaError_t e =
-      vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_c, tp,
-                       static_cast<int>(2 * clusters), s);
+      vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c,
+                       tp, static_cast<int>(2 * clusters), s);
   if (e != cudaSuccess) return GGEMM_VARK_ECUDA;
   return GGEMM_VARK_OK;
 }

@@ -379,18 +379,25 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 // Descriptors
 // ---------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor (sm_100 format): start address, leading/stride byte offsets
-// (16-byte units), version 1, 128-byte swizzle. For an MN-major 128B-swizzled operand the
-// leading offset is the distance between 128-element MN blocks and the stride offset the
-// distance between 8-row K groups.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// (16-byte units), version 1, layout (swizzle) type in bits 61-63: 2 = 128-byte, 4 = 64-byte,
+// 6 = 32-byte swizzle. For an MN-major swizzled operand the leading offset is the distance
+// between MN blocks of one swizzle width (128, 64 or 32 bytes) and the stride offset the
+// distance between 8-row K groups (8 x the swizzle width when rows are packed).
+constexpr uint64_t kSmemSw128 = 2, kSmemSw32 = 6;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint64_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;  // descriptor version for sm_100
-  d |= 2ull << 61;  // SWIZZLE_128B
+  d |= layout << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  return smem_desc(saddr, lbo_bytes, sbo_bytes, kSmemSw128);
 }
 
 // Instruction descriptor for kind::f8f6f4 with fp32 accumulation.

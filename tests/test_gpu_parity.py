@@ -82,7 +82,10 @@ def test_ragged_groups(lens, path):
                                    # last column tile widths 64, 96, 224, 32, 192 (transposed
                                    # items; 256 x 192 is the MoE layer test's weight gradient)
                                    (2880, 2880), (112, 96), (304, 480), (48, 224), (512, 32),
-                                   (256, 192)])
+                                   (256, 192),
+                                   # last row tile of 32 or 64 rows, or OUT_M < 32: B through
+                                   # the narrow 32-byte boxes
+                                   (288, 256), (320, 384), (16, 304)])
 @pytest.mark.parametrize("path", TC_PATHS)
 def test_tile_edges(shape, path):
     OUT_M, OUT_N = shape

@@ -131,6 +131,19 @@ CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// Narrow-box maps of an operand (boxes {w, box_tokens} and {w, 32}, w-byte swizzle); w = 0 (no
+// narrow items) still encodes valid 32-byte maps, which the kernel never loads through.
+CUresult encode_narrow(CUtensorMap* map, CUtensorMap* map32, const void* base, int32_t features,
+                       uint64_t tokens, int32_t pitch, uint32_t box_tokens, int32_t w) {
+  const uint32_t bw = w == 64 ? 64u : 32u;
+  const CUtensorMapSwizzle sw = w == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUresult r = encode_2d_u8(map, base, static_cast<uint64_t>(features), tokens,
+                                  static_cast<uint64_t>(pitch), box_tokens, bw, sw);
+  if (r != CUDA_SUCCESS) return r;
+  return encode_2d_u8(map32, base, static_cast<uint64_t>(features), tokens,
+                      static_cast<uint64_t>(pitch), 32, bw, sw);
+}
+
 // C as a 3-D bf16 tensor {OUT_N, OUT_M, G}; the box and swizzle follow the kernel's epilogue.
 CUresult encode_c(CUtensorMap* map, void* c, int32_t G, int32_t OUT_M, int32_t OUT_N,
                   int32_t scg, int32_t scm, uint32_t box_cols, uint32_t box_rows,
@@ -225,20 +238,23 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
                    static_cast<uint64_t>(slm), box_tokens) != CUDA_SUCCESS ||
       enc_c != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
-  // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the LHS of
-  // items with at most 64 C rows through narrow boxes.
-  CUtensorMap map_rhs32, map_lhs32, map_lhs_n, map_lhs32_n;
-  const uint32_t nw = static_cast<uint32_t>(vark::PAIR_NARROW_W);
+  // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the B of its
+  // last row tile (LHS) and transposed last column tile (RHS) through narrow boxes when their
+  // B halves fit in 32 or 64 bytes.
+  CUtensorMap map_rhs32, map_lhs32, map_lhs_n, map_lhs32_n, map_rhs_n, map_rhs32_n;
+  const int32_t last_rows = OUT_M - vark::PAIR_ROWS_MAX * (row_tiles - 1);
+  const int32_t last_cols = OUT_N - vark::PAIR_COLS * (col_tiles - 1);
+  const int32_t bw_lhs = vark::pair_narrow_width((last_rows + 31) & ~31);
+  const int32_t bw_rhs =
+      last_cols < vark::PAIR_COLS ? vark::pair_narrow_width((last_cols + 31) & ~31) : 0;
   if (pair && (encode_2d_u8(&map_rhs32, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
                             static_cast<uint64_t>(srm), 32) != CUDA_SUCCESS ||
                encode_2d_u8(&map_lhs32, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
                             static_cast<uint64_t>(slm), 32) != CUDA_SUCCESS ||
-               encode_2d_u8(&map_lhs_n, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                            static_cast<uint64_t>(slm), box_tokens, nw,
-                            CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
-               encode_2d_u8(&map_lhs32_n, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                            static_cast<uint64_t>(slm), 32, nw,
-                            CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS))
+               encode_narrow(&map_lhs_n, &map_lhs32_n, lhs_map_base, OUT_M, token_dim, slm,
+                             box_tokens, bw_lhs) != CUDA_SUCCESS ||
+               encode_narrow(&map_rhs_n, &map_rhs32_n, rhs_map_base, OUT_N, token_dim, srm,
+                             box_tokens, bw_rhs) != CUDA_SUCCESS))
     return GGEMM_VARK_ELAYOUT;
 
   vark::TcParams tp;
@@ -257,11 +273,13 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = scg;
   tp.stride_cm = scm;
+  tp.bw_lhs = pair ? bw_lhs : 0;
+  tp.bw_rhs = pair ? bw_rhs : 0;
   cudaError_t e;
   if (pair) {
     const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;
-    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c,
-                         tp, static_cast<int>(2 * clusters), s);
+    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n,
+                         map_rhs_n, map_rhs32_n, map_c, tp, static_cast<int>(2 * clusters), s);
   } else {
     const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
     e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);

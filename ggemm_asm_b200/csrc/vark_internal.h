@@ -59,6 +59,8 @@ struct TcParams {
   uint16_t* c;           // C (bf16 bits) and its element strides, for direct stores
   int64_t stride_cg;
   int64_t stride_cm;
+  int32_t bw_lhs;        // pair kernel: width in bytes (32 or 64) of the narrow LHS maps, 0: none
+  int32_t bw_rhs;        // pair kernel: the same for the narrow RHS maps
 };
 
 // Dynamic shared memory the tcgen05 kernel needs (bytes, including alignment slack).
@@ -94,12 +96,16 @@ cudaError_t tc_set_attributes();
 size_t tc2_smem_bytes();
 // map_lhs / map_rhs: 2-D u8 {features, tokens}, box {128, PAIR_TOKENS}, 128-byte swizzle.
 // map_lhs32 / map_rhs32: the same operands with 32-token boxes (a group's ragged last K step).
-// map_lhs_n / map_lhs32_n: LHS with boxes {PAIR_NARROW_W, PAIR_TOKENS} and {PAIR_NARROW_W, 32},
-// 32-byte swizzle, for items whose MMA N is at most 2 * PAIR_NARROW_W.
-constexpr int PAIR_NARROW_W = 32;
+// map_lhs_n / map_lhs32_n and map_rhs_n / map_rhs32_n: boxes {w, PAIR_TOKENS} and {w, 32} with
+// the w-byte swizzle, w = p.bw_lhs / p.bw_rhs (32 or 64; any valid map when 0). An item whose
+// B half (MMA N / 2) fits in w bytes loads B through them: the last row tile (B = LHS) and the
+// transposed last column tile (B = RHS).
+// Narrow width for a last tile of MMA N = n: 32 or 64 bytes when N / 2 fits, else 0.
+inline int32_t pair_narrow_width(int32_t n) { return n <= 64 ? 32 : (n <= 128 ? 64 : 0); }
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
                        const CUtensorMap& map_lhs_n, const CUtensorMap& map_lhs32_n,
+                       const CUtensorMap& map_rhs_n, const CUtensorMap& map_rhs32_n,
                        const CUtensorMap& map_c, const TcParams& p, int grid,
                        cudaStream_t stream);
 cudaError_t tc2_set_attributes();

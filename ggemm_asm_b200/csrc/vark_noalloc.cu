@@ -158,16 +158,29 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   const int64_t token_limit =
       m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
   const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
-  CUtensorMap map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c;
-  const uint32_t nw = static_cast<uint32_t>(vark::PAIR_NARROW_W);
+  CUtensorMap map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n,
+      map_rhs32_n, map_c;
+  // Narrow B boxes for the last row tile (LHS) and the transposed last column tile (RHS).
+  const int32_t last_rows = OUT_M - vark::PAIR_ROWS_MAX * (row_tiles - 1);
+  const int32_t last_cols = OUT_N - vark::PAIR_COLS * (col_tiles - 1);
+  const int32_t bw_lhs = vark::pair_narrow_width((last_rows + 31) & ~31);
+  const int32_t bw_rhs =
+      last_cols < vark::PAIR_COLS ? vark::pair_narrow_width((last_cols + 31) & ~31) : 0;
+  const uint32_t wl = bw_lhs == 64 ? 64u : 32u, wr = bw_rhs == 64 ? 64u : 32u;
+  const CUtensorMapSwizzle swl = wl == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapSwizzle swr = wr == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   if (encode_operand(&map_lhs, lhs, OUT_M, token_dim, stride_lhs_m) != CUDA_SUCCESS ||
       encode_operand(&map_rhs, rhs, OUT_N, token_dim, stride_rhs_m) != CUDA_SUCCESS ||
       encode_operand(&map_lhs32, lhs, OUT_M, token_dim, stride_lhs_m, 32) != CUDA_SUCCESS ||
       encode_operand(&map_rhs32, rhs, OUT_N, token_dim, stride_rhs_m, 32) != CUDA_SUCCESS ||
-      encode_operand(&map_lhs_n, lhs, OUT_M, token_dim, stride_lhs_m, vark::PAIR_TOKENS, nw,
-                     CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
-      encode_operand(&map_lhs32_n, lhs, OUT_M, token_dim, stride_lhs_m, 32, nw,
-                     CU_TENSOR_MAP_SWIZZLE_32B) != CUDA_SUCCESS ||
+      encode_operand(&map_lhs_n, lhs, OUT_M, token_dim, stride_lhs_m, vark::PAIR_TOKENS, wl,
+                     swl) != CUDA_SUCCESS ||
+      encode_operand(&map_lhs32_n, lhs, OUT_M, token_dim, stride_lhs_m, 32, wl, swl) !=
+          CUDA_SUCCESS ||
+      encode_operand(&map_rhs_n, rhs, OUT_N, token_dim, stride_rhs_m, vark::PAIR_TOKENS, wr,
+                     swr) != CUDA_SUCCESS ||
+      encode_operand(&map_rhs32_n, rhs, OUT_N, token_dim, stride_rhs_m, 32, wr, swr) !=
+          CUDA_SUCCESS ||
       encode_out(&map_c, c, G, OUT_M, OUT_N, stride_cg, stride_cm) != CUDA_SUCCESS)
     return GGEMM_VARK_ELAYOUT;
 
@@ -195,10 +208,12 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = stride_cg;
   tp.stride_cm = stride_cm;
+  tp.bw_lhs = bw_lhs;
+  tp.bw_rhs = bw_rhs;
   const int64_t clusters = items < d->sm_count / 2 ? items : d->sm_count / 2;
   const cudaError_t e =
-      vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c,
-                       tp, static_cast<int>(2 * clusters), s);
+      vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n,
+                       map_rhs32_n, map_c, tp, static_cast<int>(2 * clusters), s);
   if (e != cudaSuccess) return GGEMM_VARK_ECUDA;
   return GGEMM_VARK_OK;
 }

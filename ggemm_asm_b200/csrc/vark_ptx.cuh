@@ -383,7 +383,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 // 6 = 32-byte swizzle. For an MN-major swizzled operand the leading offset is the distance
 // between MN blocks of one swizzle width (128, 64 or 32 bytes) and the stride offset the
 // distance between 8-row K groups (8 x the swizzle width when rows are packed).
-constexpr uint64_t kSmemSw128 = 2, kSmemSw32 = 6;
+constexpr uint64_t kSmemSw128 = 2, kSmemSw64 = 4, kSmemSw32 = 6;
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
                                               uint32_t sbo_bytes, uint64_t layout) {
   uint64_t d = 0;

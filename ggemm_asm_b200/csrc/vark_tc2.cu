@@ -81,12 +81,10 @@ constexpr int ST = PAIR_STAGES;
 constexpr uint32_t BOX_BYTES = 128 * TK;                 // one operand box per CTA
 constexpr int SPB = TK / 32;                             // K steps (MMAs) per full stage
 constexpr uint32_t TAIL_BYTES = 128 * 32;                // one operand's 32-token tail chunk
-// Narrow B: an item whose MMA N is at most 64 (N/2 <= 32 C rows per CTA, e.g. the last row tile
-// at OUT_M = 11 * 256 + 64) loads B in boxes 32 bytes wide with the 32-byte swizzle instead of
-// 128 wide, which were mostly past OUT_M (zero fill) yet took the same TMA time per K step.
-constexpr uint32_t NARROW_W = PAIR_NARROW_W;             // bytes per token row of a narrow box
-constexpr uint32_t NBOX_BYTES = NARROW_W * TK;
-constexpr uint32_t NTAIL_BYTES = NARROW_W * 32;
+// Narrow B: the last row tile (B = LHS) or the transposed last column tile (B = RHS) whose
+// B half (MMA N / 2) fits in 32 or 64 bytes loads B in boxes that wide, with the matching
+// swizzle, instead of 128 wide: the 128-wide boxes were mostly past the operand's edge (zero
+// fill) yet took the same TMA time per K step. B's token rows are then bw bytes apart.
 constexpr uint32_t ACC_COLS = 256;                       // TMEM columns per accumulator
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NACC = 2;
@@ -161,7 +159,7 @@ struct Item {
   int64_t end;     // off_{g+1}
   bool edge;       // last, partial column tile: computed transposed (see the file comment)
   int ecols;       // edge item's MMA N: its C columns rounded up to 32
-  bool narrow;     // B loaded through the narrow (32-byte, 32-byte swizzle) boxes
+  uint32_t bw;     // B bytes per token row in shared memory: 128, or 64 / 32 (narrow maps)
 };
 
 __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool report) {
@@ -174,7 +172,9 @@ __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool re
   t.nrows = min(ITEM_ROWS, (p.OUT_M - t.m0 + 31) & ~31);
   t.edge = t.n0 + ITEM_COLS > p.OUT_N;
   t.ecols = (p.OUT_N - t.n0 + 31) & ~31;
-  t.narrow = !t.edge && t.nrows <= 2 * static_cast<int>(NARROW_W);
+  const int b_half = (t.edge ? t.ecols : t.nrows) >> 1;
+  const int nw = t.edge ? p.bw_rhs : p.bw_lhs;
+  t.bw = (nw > 0 && b_half <= nw) ? static_cast<uint32_t>(nw) : 128u;
   const int64_t lo = __ldg(p.group_offs + t.g);
   const int64_t hi = __ldg(p.group_offs + t.g + 1);
   if (lo < 0 || hi < lo || hi > p.token_limit) {
@@ -195,6 +195,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     const __grid_constant__ CUtensorMap map_rhs32,
                     const __grid_constant__ CUtensorMap map_lhs_n,
                     const __grid_constant__ CUtensorMap map_lhs32_n,
+                    const __grid_constant__ CUtensorMap map_rhs_n,
+                    const __grid_constant__ CUtensorMap map_rhs32_n,
                     const __grid_constant__ CUtensorMap map_c, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -241,6 +243,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&map_rhs32);
     tma_prefetch_desc(&map_lhs_n);
     tma_prefetch_desc(&map_lhs32_n);
+    tma_prefetch_desc(&map_rhs_n);
+    tma_prefetch_desc(&map_rhs32_n);
     tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
@@ -315,22 +319,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         ++ntail;
         const uint32_t ta = base + OFF_TAIL + tb * 2u * TAIL_BYTES;
         const int32_t y = lo + 32 * steps;
-        const uint32_t tail_b = t.narrow ? NTAIL_BYTES : TAIL_BYTES;
+        const bool nb = t.bw != 128u;
+        const uint32_t tail_b = t.bw * 32u;
         if (lane == 0) {
           mbar_arrive_expect_tx(bar_zfill, TAIL_BYTES + tail_b);
           tma_load_2d_hint(ta, t.edge ? &map_lhs32 : &map_rhs32, bar_zfill, xa, y, policy);
           tma_load_2d_hint(ta + TAIL_BYTES,
-                           t.edge ? &map_rhs32 : (t.narrow ? &map_lhs32_n : &map_lhs32),
+                           t.edge ? (nb ? &map_rhs32_n : &map_rhs32)
+                                  : (nb ? &map_lhs32_n : &map_lhs32),
                            bar_zfill, xb, y, policy);
         }
         ztail = static_cast<int>(tb);
         zkeep = static_cast<uint32_t>(ragged) * 128u;
-        zkeep_b = static_cast<uint32_t>(ragged) * (t.narrow ? NARROW_W : 128u);
+        zkeep_b = static_cast<uint32_t>(ragged) * t.bw;
         zend_b = tail_b;
       }
       const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
-      const CUtensorMap* const map_b = t.edge ? &map_rhs : (t.narrow ? &map_lhs_n : &map_lhs);
-      const uint32_t stage_bytes = BOX_BYTES + (t.narrow ? NBOX_BYTES : BOX_BYTES);
+      const bool nb = t.bw != 128u;
+      const CUtensorMap* const map_b =
+          t.edge ? (nb ? &map_rhs_n : &map_rhs) : (nb ? &map_lhs_n : &map_lhs);
+      const uint32_t stage_bytes = BOX_BYTES + t.bw * TK;
       for (int kb = 0; kb < nkb; ++kb) {
         // Neither wait depends on the pending tail: the MMA warp takes it after the item's
         // whole steps, and this stage's previous fill is older than all of them.
@@ -405,14 +413,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
         const uint32_t idesc = t.edge ? IDESC_EDGE_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
                                       : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
-        // B of K step ks in a stage: 32 token rows of 128 bytes (128-byte swizzle) or, for a
-        // narrow item, of 32 bytes (32-byte swizzle: 8-row K groups 256 bytes apart).
-        const bool narrow = t.narrow;
-        auto b_desc = [narrow](uint32_t b_stage, int ks) -> uint64_t {
-          return narrow ? smem_desc(b_stage + ks * (32u * NARROW_W), NBOX_BYTES, 8u * NARROW_W,
-                                    kSmemSw32)
-                        : smem_desc_sw128(b_stage + ks * 4096u, BOX_BYTES, 1024u);
-        };
+        // Descriptors without their start address, built once per item. A: 32 token rows of 128
+        // bytes per K step. B: 32 token rows of bw bytes with the bw-byte swizzle, 8-row K groups
+        // 8 * bw bytes apart. A K step adds its byte offset / 16 to the address field (the
+        // stage addresses stay far below the field's 2^18-byte range).
+        const uint32_t bw = t.bw;
+        const uint64_t b_layout = bw == 128u ? kSmemSw128 : (bw == 64u ? kSmemSw64 : kSmemSw32);
+        const uint64_t a_fixed = smem_desc_sw128(0u, BOX_BYTES, 1024u);
+        const uint64_t b_fixed = smem_desc(0u, BOX_BYTES, 8u * bw, b_layout);
+        const uint32_t b_step = 2u * bw;  // (32 rows * bw bytes) / 16
         for (int kb = 0; kb < nkb; ++kb) {
           if (!warp_wait(ctl, bar_full + 8 * stage, phase, 0x300u | stage)) {
             ok = false;
@@ -423,19 +432,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_stage = base + OFF_LHS + stage * BOX_BYTES;
           if (lane == 0) {
             const int ks_n = kb < nkb - 1 ? SPB : steps - SPB * (nkb - 1);
+            const uint64_t a0 = a_fixed | (a_stage >> 4);
+            const uint64_t b0 = b_fixed | (b_stage >> 4);
             if (ks_n == SPB) {
 #pragma unroll
-              for (int ks = 0; ks < SPB; ++ks) {
-                const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
-                mma_f8f6f4_pair(d_tmem, adesc, b_desc(b_stage, ks), idesc,
+              for (int ks = 0; ks < SPB; ++ks)
+                mma_f8f6f4_pair(d_tmem, a0 + ks * 256u, b0 + ks * b_step, idesc,
                                 (kb > 0 || ks > 0) ? 1u : 0u);
-              }
             } else {  // the last block: only its whole steps
-              for (int ks = 0; ks < ks_n; ++ks) {
-                const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, BOX_BYTES, 1024u);
-                mma_f8f6f4_pair(d_tmem, adesc, b_desc(b_stage, ks), idesc,
+              for (int ks = 0; ks < ks_n; ++ks)
+                mma_f8f6f4_pair(d_tmem, a0 + ks * 256u, b0 + ks * b_step, idesc,
                                 (kb > 0 || ks > 0) ? 1u : 0u);
-              }
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
           }
@@ -456,10 +463,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after_sync();
           if (lane == 0) {
             const uint32_t ta = base + OFF_TAIL + tb * 2u * TAIL_BYTES;
-            const uint64_t tb_desc =
-                narrow ? smem_desc(ta + TAIL_BYTES, NTAIL_BYTES, 8u * NARROW_W, kSmemSw32)
-                       : smem_desc_sw128(ta + TAIL_BYTES, TAIL_BYTES, 1024u);
-            mma_f8f6f4_pair(d_tmem, smem_desc_sw128(ta, TAIL_BYTES, 1024u), tb_desc, idesc,
+            const uint64_t tb_desc = b_fixed | ((ta + TAIL_BYTES) >> 4);
+            mma_f8f6f4_pair(d_tmem, a_fixed | (ta >> 4), tb_desc, idesc,
                             steps > 0 ? 1u : 0u);
             mma_commit_pair(bar_tail_empty + 8 * tb, 0x3);  // frees the tail in both CTAs
           }
@@ -651,10 +656,12 @@ size_t tc2_smem_bytes() { return SMEM_ALLOC; }
 cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
                        const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
                        const CUtensorMap& map_lhs_n, const CUtensorMap& map_lhs32_n,
+                       const CUtensorMap& map_rhs_n, const CUtensorMap& map_rhs32_n,
                        const CUtensorMap& map_c, const TcParams& p, int grid,
                        cudaStream_t stream) {
   vark_tc2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(
-      map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_c, p);
+      map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n, map_rhs32_n,
+      map_c, p);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,16 @@ constexpr uint32_t QT_CHUNK = VARK_QT_CHUNK;
 static_assert(QT_CHUNK % 16 == 0, "chunk: whole 16-byte vectors");
 constexpr int QT_STAGES = VARK_QT_STAGES;
 constexpr size_t QT_SMEM = static_cast<size_t>(QT_STAGES) * QT_CHUNK + 2 * QT_STAGES * 8 + 128;
+// The same shared memory as a ring of 2 chunks of up to 1.5 x QT_CHUNK. The host takes it when a
+// CTA's average slice of a unit fits in two such chunks. At the gate_up shapes x (slices of
+// ~159 KB) takes it: 0.299 ms against 0.328 ms with 64 KB x 3, measured in one process; dy
+// (~318 KB), for which 96 KB x 2 measured 0.552 ms against 0.499, keeps 64 KB x 3.
+// The kernel is instantiated per ring (NS stages of ring_cap<NS>() bytes): the stage index and
+// phase of every chunk then come from divisions by a constant.
+constexpr int QT_STAGES_WIDE = 2;
+template <int NS>
+constexpr uint32_t ring_cap() { return static_cast<uint32_t>(QT_STAGES * QT_CHUNK / NS); }
+static_assert(ring_cap<QT_STAGES_WIDE>() % 16 == 0 && QT_STAGES_WIDE <= QT_STAGES, "wide ring");
 
 struct QuantParams {
   const uint8_t* x;          // bf16 rows
@@ -439,22 +449,26 @@ struct Slice {
   }
 };
 
-// Equal chunks of at most QT_CHUNK bytes over len bytes (len a multiple of 16).
+// Equal chunks of at most CAP bytes over len bytes (len and CAP multiples of 16; CAP is a
+// constant, so the divisions are by constants).
+template <uint32_t CAP>
 __device__ __forceinline__ void cut_slice(Slice& sl) {
+  constexpr int64_t cap = CAP;
   const int64_t len = sl.b1 - sl.b0;
   if (len <= 0) {
     sl.n = 0;
-    sl.cb = QT_CHUNK;
+    sl.cb = CAP;
     return;
   }
-  const int64_t n0 = (len + QT_CHUNK - 1) / QT_CHUNK;
-  const int64_t cb = ((len + n0 - 1) / n0 + 15) / 16 * 16;  // <= QT_CHUNK (a multiple of 16)
+  const int64_t n0 = (len + cap - 1) / cap;
+  const int64_t cb = ((len + n0 - 1) / n0 + 15) / 16 * 16;  // <= cap (a multiple of 16)
   sl.cb = static_cast<uint32_t>(cb);
   sl.n = (len + cb - 1) / cb;  // every chunk non-empty
 }
 
+template <int NS>
 __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
-  Slice sl{0, 0, false, 0, QT_CHUNK};
+  Slice sl{0, 0, false, 0, ring_cap<NS>()};
   if (w < 0 || w >= p.units) return sl;
   int64_t lo, hi;
   if (!unit_rows(p, w, &lo, &hi) || hi == lo) return sl;
@@ -464,7 +478,7 @@ __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
   sl.b0 = lo * p.stride_x + v0 * 16;
   sl.b1 = lo * p.stride_x + v1 * 16;
   sl.unit_ok = true;
-  cut_slice(sl);
+  cut_slice<ring_cap<NS>()>(sl);
   return sl;
 }
 
@@ -498,6 +512,7 @@ __device__ __forceinline__ void consumers_sync() {
 // Producer warp, lane 0: issue every chunk in the consumers' order once its stage is free;
 // before returning, let the last copy of every stage land (the CTA's shared memory must outlive
 // it).
+template <int NS>
 struct Producer {
   const QuantParams& p;
   uint32_t stage0;
@@ -508,9 +523,10 @@ struct Producer {
   bool ok = true;
   __device__ __forceinline__ void issue(const Slice& sl, int64_t t, bool first_read) {
     if (!ok) return;
-    const int k = static_cast<int>(n % QT_STAGES);
-    if (n >= QT_STAGES &&
-        !wait_bar(smem_u32(empty + k), static_cast<uint32_t>((n / QT_STAGES - 1) & 1),
+    constexpr int64_t ns = NS;
+    const int k = static_cast<int>(n % ns);
+    if (n >= ns &&
+        !wait_bar(smem_u32(empty + k), static_cast<uint32_t>((n / ns - 1) & 1),
                   p.timeout_ns)) {
       report_timeout(p, 0x53000000u);
       ok = false;
@@ -519,16 +535,16 @@ struct Producer {
     const uint32_t bytes = sl.chunk_bytes(t);
     const uint32_t bar = smem_u32(full + k);
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_load_1d(stage0 + k * QT_CHUNK, p.x + sl.b0 + sl.chunk_offset(t), bytes, bar,
+    bulk_load_1d(stage0 + k * ring_cap<NS>(), p.x + sl.b0 + sl.chunk_offset(t), bytes, bar,
                  first_read ? pol_keep : pol_last);
     ++n;
   }
   __device__ void run() {
-    Slice a = slice_info(p, 0);
+    Slice a = slice_info<NS>(p, 0);
     for (int64_t t = 0; t < a.chunks(); ++t) issue(a, t, true);
     for (int s = 1; s <= p.units && ok; ++s) {
-      const Slice b = slice_info(p, s - 1);
-      a = slice_info(p, s);
+      const Slice b = slice_info<NS>(p, s - 1);
+      a = slice_info<NS>(p, s);
       const int64_t na = a.chunks(), nb = b.chunks();
       for (int64_t ta = 0, tb = 0; ta < na || tb < nb;) {
         if (amax_next(ta, tb, na, nb))
@@ -537,14 +553,15 @@ struct Producer {
           issue(b, tb++, false);
       }
     }
-    for (int64_t c = n > QT_STAGES ? n - QT_STAGES : 0; c < n; ++c)
-      wait_bar(smem_u32(full + static_cast<int>(c % QT_STAGES)),
-               static_cast<uint32_t>((c / QT_STAGES) & 1), p.timeout_ns);
+    constexpr int64_t ns = NS;
+    for (int64_t c = n > ns ? n - ns : 0; c < n; ++c)
+      wait_bar(smem_u32(full + static_cast<int>(c % ns)), static_cast<uint32_t>((c / ns) & 1),
+               p.timeout_ns);
   }
 };
 
 // Consumer warps (kQtThreads threads): the same chunk order as the producer.
-template <bool E5M2>
+template <bool E5M2, int NS>
 struct Consumer {
   const QuantParams& p;
   uint8_t* stages;
@@ -561,13 +578,14 @@ struct Consumer {
 
   // Wait for chunk j in its stage (warp-uniform verdict); returns the stage or nullptr.
   __device__ __forceinline__ const uint4* acquire(int* k_out) {
-    const int k = static_cast<int>(j % QT_STAGES);
+    constexpr int64_t ns = NS;
+    const int k = static_cast<int>(j % ns);
     *k_out = k;
     if (!__all_sync(0xffffffffu, wait_bar(smem_u32(full + k),
-                                          static_cast<uint32_t>((j / QT_STAGES) & 1),
+                                          static_cast<uint32_t>((j / ns) & 1),
                                           p.timeout_ns)))
       return nullptr;
-    return reinterpret_cast<const uint4*>(stages + k * QT_CHUNK);
+    return reinterpret_cast<const uint4*>(stages + k * ring_cap<NS>());
   }
   __device__ __forceinline__ void release(int k) {
     __syncwarp();
@@ -654,13 +672,13 @@ struct Consumer {
     p.scales[w] = 1.0f;  // invalid or empty unit
   }
   __device__ __forceinline__ void run() {
-    Slice a = slice_info(p, 0);
+    Slice a = slice_info<NS>(p, 0);
     note_unit(0, a);
     for (int64_t t = 0; t < a.chunks(); ++t) amax_chunk(a, t);
     if (a.unit_ok && !finish_amax(0)) return;
     for (int s = 1; s <= p.units; ++s) {
-      const Slice b = slice_info(p, s - 1);
-      a = slice_info(p, s);
+      const Slice b = slice_info<NS>(p, s - 1);
+      a = slice_info<NS>(p, s);
       if (s < p.units) note_unit(s, a);
       const bool need_scale = b.unit_ok && (b.b1 > b.b0 || blockIdx.x == 0);
       bool have_scale = false;
@@ -683,7 +701,7 @@ struct Consumer {
   }
 };
 
-template <bool E5M2>
+template <bool E5M2, int NS>
 __global__ void __launch_bounds__(kTmaThreads) vark_quant_tma_kernel(const QuantParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
@@ -703,13 +721,13 @@ __global__ void __launch_bounds__(kTmaThreads) vark_quant_tma_kernel(const Quant
   __syncthreads();  // the only barrier with the producer warp
   if (warp == kQtWarps) {
     if (lane == 0) {
-      Producer pr{p, smem_u32(smem), full, empty, l2_policy_evict_last(),
+      Producer<NS> pr{p, smem_u32(smem), full, empty, l2_policy_evict_last(),
                   l2_policy_evict_first()};
       pr.run();
     }
     return;
   }
-  Consumer<E5M2> c{p, smem, full, empty, red, lane, warp};
+  Consumer<E5M2, NS> c{p, smem, full, empty, red, lane, warp};
   c.withhold = test_withhold(p);
   c.run();
   if (c.fail && threadIdx.x == 0) report_timeout(p, 0x52000000u);
@@ -752,8 +770,20 @@ cudaError_t quant_launch(const uint8_t* x, uint8_t* q, float* scales, const int6
   size_t smem = 0;
   int threads = kThreads;
   if (mode == 2) {
-    fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true>)
-              : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false>);
+    // Ring: two wide chunks when a CTA's average slice of a unit fits in them (known row count
+    // only), else the default ring. Either ring takes ~192 KiB of shared memory: one CTA per SM.
+    bool wide = false;
+    if (token_limit != INT64_MAX && p.units > 0) {
+      const double slice = static_cast<double>(token_limit) * static_cast<double>(stride_x_bytes) /
+                           (static_cast<double>(p.units) * sm_count);
+      wide = slice <= 2.0 * ring_cap<QT_STAGES_WIDE>();
+    }
+    if (wide)
+      fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true, QT_STAGES_WIDE>)
+                : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false, QT_STAGES_WIDE>);
+    else
+      fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true, QT_STAGES>)
+                : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false, QT_STAGES>);
     smem = QT_SMEM;
     threads = kTmaThreads;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,

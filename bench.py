@@ -23,10 +23,17 @@ fp8 quantisation of x and dy, GB/s), --op fwd --site <site> (the fixed-K grouped
 forward / data-gradient site, TFLOPS, with cuBLAS per expert beside it), --op layer (one training
 step of the FP8 MoE linear layer).
 
+Beside the headline the line carries ``other_workloads``: at N = 1 the down_wgrad and skewed-
+routing problems, and at every N the GPT-OSS-120B-shaped problem (G = 128, M_total = 1048576)
+split into contiguous expert ranges across the ranks (strong scaling; max over ranks, with the
+per-rank times and token counts).
+
 --impl reference: the reference's own implementation of the path cannot run here (AMD gfx950
 code object + a Triton kernel from the absent primus_turbo package), so the reference arm
 times the CPU restatement of its algorithm (oracle/, torch fp32 dequantise + matmul per expert)
-on all host threads, one expert per step, on rank 0 only.
+on all host threads, rank 0 only. One step multiplies the first quarter of every expert's tokens
+(all experts, in proportion), the same sample the repo arm's ``cpu_baseline`` times, and the
+line carries the same metric string as the repo arm.
 """
 from __future__ import annotations
 
@@ -68,6 +75,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-other", action="store_true",
+                    help="skip the down / skew / 120B-split workloads printed beside the headline")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="approximate CPU-baseline sample budget")
     ap.add_argument("--groups", type=int, default=None,
@@ -197,24 +206,55 @@ def build_problem(args, rank, world, device):
     return p, "weak"
 
 
-def cpu_oracle_rate(p_cpu, budget_s: float, steps: int | None = None):
-    """Time the oracle (torch CPU fp32, all threads) on whole experts; returns (TFLOPS, sample)."""
+def workload_name(config: str) -> str:
+    """The wgrad workload a config measures (shard120b and ref_exp are gate_up-shaped)."""
+    return "gate_up" if config in ("gate_up", "ref_exp", "shard120b") else config
+
+
+def metric_name(config: str) -> str:
+    """The metric string both arms print for a config (the driver compares them verbatim)."""
+    return f"{workload_name(config)}_wgrad FP8 TFLOPS (whole job)"
+
+
+# Fraction of every expert's tokens that one CPU sample step multiplies: all experts, in
+# proportion to their sizes, so the sample has the workload's expert mix (about 0.6 s of
+# 16-thread CPU time at the gate_up shape).
+CPU_SAMPLE_FRAC = 0.25
+
+
+def cpu_sample_step(p_cpu, frac: float = CPU_SAMPLE_FRAC) -> float:
+    """One step of the CPU restatement (oracle/, torch CPU fp32 dequantise + matmul) over the
+    first ceil(frac * K_g) tokens of every expert g; returns the FLOPs done."""
     from oracle import vark_oracle as vo
 
-    order = np.argsort(-p_cpu.lens)  # big experts first: fewer, longer matmuls
-    done_flops, t_total, groups = 0.0, 0.0, []
-    for i, g in enumerate([int(x) for x in order if p_cpu.lens[x] > 0]):
+    offs = p_cpu.group_offs.clone()
+    flops = 0.0
+    for g in range(p_cpu.G):
+        k = int(np.ceil(frac * float(p_cpu.lens[g])))
+        if k == 0:
+            continue
+        sub = offs.clone()
+        sub[g + 1] = offs[g] + k  # the oracle reads only [offs[g], offs[g+1]) for group g
+        vo.wgrad_torch(p_cpu.lhs, p_cpu.rhs, p_cpu.lhs_scale, p_cpu.rhs_scale, sub, groups=[g])
+        flops += 2.0 * k * p_cpu.OUT_M * p_cpu.OUT_N
+    return flops
+
+
+def cpu_sample_desc(p_cpu, frac: float = CPU_SAMPLE_FRAC) -> str:
+    return (f"every step: the first {frac:.0%} of every expert's tokens ({p_cpu.G} experts, "
+            f"{int(np.ceil(frac * p_cpu.lens).sum())} of {int(p_cpu.lens.sum())} tokens) of the "
+            f"same problem, torch CPU fp32 dequantise + matmul per expert")
+
+
+def cpu_oracle_rate(p_cpu, budget_s: float):
+    """Time the CPU sample steps until `budget_s` has passed; returns (TFLOPS, sample, secs)."""
+    done_flops, t_total, steps = 0.0, 0.0, 0
+    while t_total < budget_s:
         t0 = time.perf_counter()
-        vo.wgrad_torch(p_cpu.lhs, p_cpu.rhs, p_cpu.lhs_scale, p_cpu.rhs_scale, p_cpu.group_offs,
-                       groups=[g])
+        done_flops += cpu_sample_step(p_cpu)
         t_total += time.perf_counter() - t0
-        done_flops += 2.0 * float(p_cpu.lens[g]) * p_cpu.OUT_M * p_cpu.OUT_N
-        groups.append(g)
-        if (steps is not None and i + 1 >= steps) or (steps is None and t_total >= budget_s):
-            break
-    sample = (f"{len(groups)} of {p_cpu.G} experts ({int(sum(p_cpu.lens[groups]))} tokens) of "
-              f"the same problem, torch CPU fp32 dequantise+matmul per expert")
-    return done_flops / t_total / 1e12, sample, t_total
+        steps += 1
+    return done_flops / t_total / 1e12, f"{steps} steps; " + cpu_sample_desc(p_cpu), t_total
 
 
 def run_reference(args):
@@ -223,25 +263,21 @@ def run_reference(args):
     if rank != 0:
         return
     from ggemm_asm_b200 import inputs
-    from oracle import vark_oracle as vo
 
     torch.set_num_threads(os.cpu_count() or 1)
-    name = "gate_up" if args.config in ("ref_exp", "shard120b") else args.config
+    name = workload_name(args.config)
     p = inputs.make_problem(name, seed=args.seed, device="cpu")
-    live = [int(g) for g in np.argsort(-p.lens) if p.lens[g] > 0]
-    for i in range(args.warmup):
-        vo.wgrad_torch(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, groups=[live[i % len(live)]])
+    for _ in range(args.warmup):
+        cpu_sample_step(p)
     flops, t = 0.0, 0.0
-    for i in range(args.steps):
-        g = live[i % len(live)]
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        vo.wgrad_torch(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs, groups=[g])
+        flops += cpu_sample_step(p)
         t += time.perf_counter() - t0
-        flops += 2.0 * float(p.lens[g]) * p.OUT_M * p.OUT_N
     v = flops / t / 1e12
     cores = torch.get_num_threads()
-    sample = f"one expert per step (experts in size order) of config {name}"
-    line = {"impl": "reference", "metric": f"{name}_wgrad FP8 TFLOPS (CPU restatement)",
+    sample = cpu_sample_desc(p)
+    line = {"impl": "reference", "metric": metric_name(args.config),
             "value": v, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -669,6 +705,63 @@ def main():
     value = flops_total / (ms * 1e-3) / 1e12
     if _lib.read_status(clear=True) != 0:
         raise SystemExit("device status flags set during the timed region")
+    fp8_peak, _hbm, peak_src = measured_peaks()
+
+    # ---- the other wgrad workloads, each timed like the headline (outside its timed region) --
+    # N = 1: down_wgrad and the skewed-routing stress problem (BASELINE configs 2 and 3). Every
+    # N: the GPT-OSS-120B-shaped problem (config 4: G = 128, M_total = 1048576) split into
+    # contiguous expert ranges across the ranks (strong scaling; at N = 1 the whole problem).
+    def time_steps(fn, steps):
+        for _ in range(3):
+            fn()
+        barrier()
+        ev0.record(stream)
+        for _ in range(steps):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return ev0.elapsed_time(ev1) / steps
+
+    other = {}
+    if args.config == "gate_up" and not args.no_other:
+        from ggemm_asm_b200 import inputs
+
+        names = (["down", "skew"] if world == 1 else []) + ["shard120b"]
+        for name in names:
+            if name == "shard120b":
+                q, _ = build_problem(argparse.Namespace(**{**vars(args), "config": name}), rank,
+                                     world, device)
+            else:
+                q = inputs.make_problem(name, seed=args.seed, device=device)
+            qo = torch.empty(q.G, q.OUT_M, q.OUT_N, dtype=torch.bfloat16, device=device)
+            q_ms = time_steps(lambda: variable_k_wgrad(q.lhs, q.rhs, q.lhs_scale, q.rhs_scale,
+                                                       q.group_offs, out=qo), args.steps)
+            if name == "shard120b":
+                per_ms = _gather_over_ranks(pg, q_ms, device)
+                per_tok = _gather_over_ranks(pg, float(q.lens.sum()), device)
+                q_flops = 2.0 * sum(per_tok) * q.OUT_M * q.OUT_N
+                t = max(per_ms)
+                other["shard120b_strong"] = {
+                    "value": q_flops / (t * 1e-3) / 1e12, "unit": "TFLOPS",
+                    "per_gpu": q_flops / (t * 1e-3) / 1e12 / world, "ms_per_step": t,
+                    "per_rank_ms": per_ms, "per_rank_tokens": [int(v) for v in per_tok],
+                    "per_rank_tflops": [2.0 * k * q.OUT_M * q.OUT_N / (m * 1e-3) / 1e12
+                                        for k, m in zip(per_tok, per_ms)],
+                    "scaling": "strong", "steps": args.steps,
+                    "config": {"G": 128, "M_total": 1048576, "OUT_M": q.OUT_M,
+                               "OUT_N": q.OUT_N, "split": "contiguous expert ranges"}}
+            else:
+                other[f"{name}_wgrad"] = {
+                    "value": q.flops / (q_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+                    "ms_per_step": q_ms, "steps": args.steps,
+                    "frac": q.flops / (q_ms * 1e-3) / 1e12 / fp8_peak,
+                    "config": {"G": q.G, "M_total": q.M_total, "OUT_M": q.OUT_M,
+                               "OUT_N": q.OUT_N}}
+            del q, qo
+            torch.cuda.empty_cache()
+        if _lib.read_status(clear=True) != 0:
+            raise SystemExit("device status flags set in the other workloads")
 
     # ---- end-to-end: pinned host inputs -> device -> kernel -> result back to the host ------
     # Through the host-buffer entry point (HostWgrad): per step, the H2D copy of LHS, RHS, scales
@@ -742,7 +835,6 @@ def main():
                           "api": "copy in, one grouped_gemm_fp8_tensorwise_variable_k, copy out"}}
 
     # ---- roofline of the dominant kernel ------------------------------------------------------
-    fp8_peak, _hbm, peak_src = measured_peaks()
     achieved = flops_local / (ms_local * 1e-3) / 1e12
     workload = f"{args.config}"
     roofline = {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
@@ -760,12 +852,12 @@ def main():
         pc = inputs.Problem(**{**p.__dict__}).to("cpu")
         rate, sample, secs = cpu_oracle_rate(pc, args.cpu_seconds)
         cpu = {"value": rate, "unit": "TFLOPS", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": sample + f"; {secs:.1f} s", "os_cpu_count": os.cpu_count()}
+               "sample": sample + f"; {secs:.1f} s", "os_cpu_count": os.cpu_count(),
+               "same_as": "bench.py --impl reference (same sample steps)"}
 
     if rank == 0:
         line = {
-            "metric": "gate_up_wgrad FP8 TFLOPS (whole job) and fraction of dense FP8 peak"
-            if args.config in ("gate_up", "shard120b", "ref_exp") else f"{args.config}_wgrad FP8 TFLOPS",
+            "metric": metric_name(args.config),
             "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
             "scaling": scaling,
@@ -782,11 +874,22 @@ def main():
             "clocks": clocks, "clocks_sustained_untimed": clocks_sustained,
             "gpu_launches": args.steps,
             "gpu_launches_e2e": None if e2e is None else e2e["steps"],
+            "other_workloads": other,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
+
+
+def _gather_over_ranks(pg, x: float, device) -> list[float]:
+    """x from every rank, in rank order (outside any timed region)."""
+    if pg is None:
+        return [x]
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    out = torch.empty(pg.get_world_size(), dtype=torch.float64, device=device)
+    pg.all_gather_into_tensor(out, t)
+    return [float(v) for v in out.tolist()]
 
 
 def _sum_over_ranks(pg, x: float, device) -> float:

@@ -14,6 +14,8 @@ Public API:
   moe.GroupedLinearFP8 / grouped_linear_fp8  FP8 MoE expert linear layer with autograd (forward,
                                           data gradient and weight gradient on these kernels)
   inputs / sharding                       seeded problems and expert sharding for 1..8 GPUs
+  ops                                     the kernels as torch operators (torch.ops.ggemm.*) with
+                                          fake implementations, so they trace
 The C ABI itself is declared in include/ggemm_vark.h and lives in libggemm_vark.so.
 """
 from .grouped_gemm import (  # noqa: F401
@@ -25,5 +27,6 @@ from .grouped_gemm import (  # noqa: F401
 from ._lib import VarkError, read_status  # noqa: F401
 from .grouped_fwd import grouped_gemm_fp8_tensorwise  # noqa: F401
 from .quantize import quantize_fp8  # noqa: F401
+from . import ops  # noqa: F401,E402  (registers torch.ops.ggemm.*)
 
 __version__ = "0.1.0"

@@ -25,6 +25,12 @@ ETOO_LARGE = 8
 DEV_BAD_OFFS = 0x1
 DEV_TIMEOUT = 0x2
 
+# Status block words (GGEMM_VARK_STATUS_WORD_*).
+STATUS_WORD_BITS = 0
+STATUS_WORD_SITE = 1
+STATUS_WORD_LHS_ROWS = 4
+STATUS_WORD_RHS_ROWS = 5
+
 PATH_AUTO = 0
 PATH_TCGEN05 = 1
 PATH_SIMT = 2
@@ -53,6 +59,9 @@ SIGNATURES = {
     "ggemm_vark_quantize_fp8": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                                _i32, _i64, _vp, _vp, _u64, _vp]),
     "ggemm_vark_read_status": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
+    "ggemm_vark_read_status_stream": (ctypes.c_int, [_vp, ctypes.c_int,
+                                                     ctypes.POINTER(ctypes.c_uint32), _i32, _vp]),
+    "ggemm_vark_device_bytes": (ctypes.c_int, [_i32, ctypes.POINTER(ctypes.c_uint64)]),
     "ggemm_vark_tc_supported": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                                                _i32]),
     "ggemm_vark_strerror": (ctypes.c_char_p, [ctypes.c_int]),
@@ -109,3 +118,21 @@ def read_status(status_ptr: int | None = None, clear: bool = False) -> int:
     check(lib().ggemm_vark_read_status(status_ptr, 1 if clear else 0, ctypes.byref(bits)),
           "ggemm_vark_read_status")
     return int(bits.value)
+
+
+def read_status_words(status_ptr: int | None = None, nwords: int = 8, clear: bool = False,
+                      stream: int | None = None) -> list[int]:
+    """The first `nwords` words of a status block, read in the order of `stream` (None = the
+    legacy default stream); only that stream is waited for."""
+    words = (ctypes.c_uint32 * 8)()
+    check(lib().ggemm_vark_read_status_stream(status_ptr, 1 if clear else 0, words, nwords,
+                                              stream),
+          "ggemm_vark_read_status_stream")
+    return [int(words[i]) for i in range(nwords)]
+
+
+def device_bytes(device: int) -> int:
+    """Device memory the library has allocated on `device` (its status block, once set up)."""
+    n = ctypes.c_uint64(0)
+    check(lib().ggemm_vark_device_bytes(device, ctypes.byref(n)), "ggemm_vark_device_bytes")
+    return int(n.value)

@@ -36,7 +36,6 @@ struct DeviceState {
 
 std::mutex g_mutex;
 DeviceState g_dev[kMaxDevices];
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int fail_cuda(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
@@ -75,14 +74,7 @@ int get_device(DeviceState** out, int* dev_out) {
       return fail_cuda(e);
     }
     s.status = static_cast<uint32_t*>(blk);
-    if (g_encode == nullptr) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q;
-      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
-        return fail_cuda(e == cudaSuccess ? cudaErrorSymbolNotFound : e);
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+    if (vark::tensor_map_encoder() == nullptr) return fail_cuda(cudaErrorSymbolNotFound);
     s.ready = true;
   }
   *out = &s;
@@ -126,9 +118,10 @@ CUresult encode_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64
   const cuuint64_t strides[1] = {row_pitch};
   const cuuint32_t box[2] = {box_inner, box_tokens};
   const cuuint32_t estr[2] = {1, 1};
-  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const auto enc = vark::tensor_map_encoder();
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
 // Narrow-box maps of an operand (boxes {w, box_tokens} and {w, 32}, w-byte swizzle); w = 0 (no
@@ -154,9 +147,10 @@ CUresult encode_c(CUtensorMap* map, void* c, int32_t G, int32_t OUT_M, int32_t O
                                  2ull * static_cast<cuuint64_t>(scg)};
   const cuuint32_t box[3] = {box_cols, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
-  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const auto enc = vark::tensor_map_encoder();
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
 int run(const void* lhs, const void* rhs, void* c, const float* ls, const float* rs,
@@ -207,6 +201,7 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
     sp.stride_cn = scn;
     sp.token_limit = token_limit;
     sp.status = st;
+    sp.offs_bound = m_total < 0 ? 1 : 0;
     if (G > 65535) return GGEMM_VARK_ETOO_LARGE;
     cudaError_t e = vark::simt_launch(sp, s);
     return e == cudaSuccess ? GGEMM_VARK_OK : fail_cuda(e);
@@ -221,41 +216,28 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   const int64_t tiles = static_cast<int64_t>(G) * row_tiles * col_tiles;
   if (tiles > INT32_MAX) return GGEMM_VARK_ETOO_LARGE;
 
-  CUtensorMap map_rhs, map_lhs, map_c;
   // With no tokens the operand maps are never used for a load; they only need to be valid
   // descriptors, so they point at C.
   const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
-  const void* lhs_map_base = lhs != nullptr ? lhs : c;
-  const void* rhs_map_base = rhs != nullptr ? rhs : c;
-  const CUresult enc_c =
-      pair ? encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
-           : encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, vark::EPI_BOX_COLS,
-                      vark::EPI_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
-  const uint32_t box_tokens = pair ? vark::PAIR_TOKENS : vark::TILE_TOKENS;
-  if (encode_2d_u8(&map_rhs, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
-                   static_cast<uint64_t>(srm), box_tokens) != CUDA_SUCCESS ||
-      encode_2d_u8(&map_lhs, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                   static_cast<uint64_t>(slm), box_tokens) != CUDA_SUCCESS ||
-      enc_c != CUDA_SUCCESS)
+  vark::PairMaps pm;
+  CUtensorMap map_rhs, map_lhs, map_c;  // the single-CTA kernel's maps
+  if (pair) {
+    // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the B of
+    // its last row tile (LHS) and transposed last column tile (RHS) through narrow boxes when
+    // their B halves fit in 32 or 64 bytes.
+    if (!vark::encode_pair_maps(&pm, lhs, rhs, c, G, OUT_M, OUT_N, slm, srm, scg, scm,
+                                token_dim))
+      return GGEMM_VARK_ELAYOUT;
+  } else if (encode_2d_u8(&map_rhs, rhs != nullptr ? rhs : c, static_cast<uint64_t>(OUT_N),
+                          token_dim, static_cast<uint64_t>(srm), vark::TILE_TOKENS) !=
+                 CUDA_SUCCESS ||
+             encode_2d_u8(&map_lhs, lhs != nullptr ? lhs : c, static_cast<uint64_t>(OUT_M),
+                          token_dim, static_cast<uint64_t>(slm), vark::TILE_TOKENS) !=
+                 CUDA_SUCCESS ||
+             encode_c(&map_c, c, G, OUT_M, OUT_N, scg, scm, vark::EPI_BOX_COLS,
+                      vark::EPI_BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS) {
     return GGEMM_VARK_ELAYOUT;
-  // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the B of its
-  // last row tile (LHS) and transposed last column tile (RHS) through narrow boxes when their
-  // B halves fit in 32 or 64 bytes.
-  CUtensorMap map_rhs32, map_lhs32, map_lhs_n, map_lhs32_n, map_rhs_n, map_rhs32_n;
-  const int32_t last_rows = OUT_M - vark::PAIR_ROWS_MAX * (row_tiles - 1);
-  const int32_t last_cols = OUT_N - vark::PAIR_COLS * (col_tiles - 1);
-  const int32_t bw_lhs = vark::pair_narrow_width((last_rows + 31) & ~31);
-  const int32_t bw_rhs =
-      last_cols < vark::PAIR_COLS ? vark::pair_narrow_width((last_cols + 31) & ~31) : 0;
-  if (pair && (encode_2d_u8(&map_rhs32, rhs_map_base, static_cast<uint64_t>(OUT_N), token_dim,
-                            static_cast<uint64_t>(srm), 32) != CUDA_SUCCESS ||
-               encode_2d_u8(&map_lhs32, lhs_map_base, static_cast<uint64_t>(OUT_M), token_dim,
-                            static_cast<uint64_t>(slm), 32) != CUDA_SUCCESS ||
-               encode_narrow(&map_lhs_n, &map_lhs32_n, lhs_map_base, OUT_M, token_dim, slm,
-                             box_tokens, bw_lhs) != CUDA_SUCCESS ||
-               encode_narrow(&map_rhs_n, &map_rhs32_n, rhs_map_base, OUT_N, token_dim, srm,
-                             box_tokens, bw_rhs) != CUDA_SUCCESS))
-    return GGEMM_VARK_ELAYOUT;
+  }
 
   vark::TcParams tp;
   tp.group_offs = offs;
@@ -273,13 +255,13 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = scg;
   tp.stride_cm = scm;
-  tp.bw_lhs = pair ? bw_lhs : 0;
-  tp.bw_rhs = pair ? bw_rhs : 0;
+  tp.bw_lhs = pair ? pm.bw_lhs : 0;
+  tp.bw_rhs = pair ? pm.bw_rhs : 0;
+  tp.offs_bound = m_total < 0 ? 1 : 0;
   cudaError_t e;
   if (pair) {
     const int64_t clusters = tiles < dev->sm_count / 2 ? tiles : dev->sm_count / 2;
-    e = vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n,
-                         map_rhs_n, map_rhs32_n, map_c, tp, static_cast<int>(2 * clusters), s);
+    e = vark::tc2_launch(pm, tp, static_cast<int>(2 * clusters), s);
   } else {
     const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
     e = vark::tc_launch(map_rhs, map_lhs, map_c, tp, grid, s);
@@ -320,16 +302,16 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
   // A [rows, K] u8 and C [rows, N] bf16 over all M_total rows: the kernel addresses an expert's
   // rows by coordinate (off_g + row) and writes each expert's ragged last rows without TMA.
   CUtensorMap map_a, map_b, map_c;
+  const auto enc = vark::tensor_map_encoder();
   const uint64_t rows = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), rows};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(sam)};
     const cuuint32_t box[2] = {128, 128};
     const cuuint32_t estr[2] = {1, 1};
-    if (g_encode(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), dims, strides,
-                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
+    if (enc(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return GGEMM_VARK_ELAYOUT;
   }
   {
@@ -338,10 +320,9 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(sbn), static_cast<cuuint64_t>(sbg)};
     const cuuint32_t box[3] = {128, b_layout == 0 ? 128u : 256u, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (g_encode(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(b), dims, strides,
-                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
+    if (enc(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(b), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return GGEMM_VARK_ELAYOUT;
   }
   {
@@ -349,10 +330,9 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
     const cuuint64_t strides[1] = {2ull * static_cast<cuuint64_t>(scm)};
     const cuuint32_t box[2] = {32, 32};
     const cuuint32_t estr[2] = {1, 1};
-    if (g_encode(&map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c, dims, strides, box, estr,
-                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
+    if (enc(&map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return GGEMM_VARK_ELAYOUT;
   }
   vark::FwdParams fp;
@@ -371,6 +351,7 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
   fp.timeout_ns = timeout_ns != 0 ? timeout_ns : kDefaultTimeoutNs;
   fp.c = static_cast<uint16_t*>(c);
   fp.stride_cm = scm;
+  fp.offs_bound = m_total < 0 ? 1 : 0;
   // The item count depends on the group sizes, which stay on the device: one cluster per pair
   // of SMs, each walking the items round-robin (clusters without items exit at once).
   const cudaError_t e = vark::fwd2_launch(map_a, map_b, map_c, fp, 2 * (dev->sm_count / 2),
@@ -381,6 +362,50 @@ int run_fwd(const void* a, const void* b, void* c, const float* a_scale, const f
 }  // namespace
 
 namespace vark {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && p != nullptr)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_pair_maps(PairMaps* m, const void* lhs, const void* rhs, void* c, int32_t G,
+                      int32_t OUT_M, int32_t OUT_N, int32_t slm, int32_t srm, int32_t scg,
+                      int32_t scm, uint64_t token_dim) {
+  if (tensor_map_encoder() == nullptr) return false;
+  const void* lb = lhs != nullptr ? lhs : c;
+  const void* rb = rhs != nullptr ? rhs : c;
+  const int32_t row_tiles = (OUT_M + PAIR_ROWS_MAX - 1) / PAIR_ROWS_MAX;
+  const int32_t col_tiles = (OUT_N + PAIR_COLS - 1) / PAIR_COLS;
+  const int32_t last_rows = OUT_M - PAIR_ROWS_MAX * (row_tiles - 1);
+  const int32_t last_cols = OUT_N - PAIR_COLS * (col_tiles - 1);
+  m->bw_lhs = pair_narrow_width((last_rows + 31) & ~31);
+  m->bw_rhs = last_cols < PAIR_COLS ? pair_narrow_width((last_cols + 31) & ~31) : 0;
+  const uint64_t fm = static_cast<uint64_t>(OUT_M), fn = static_cast<uint64_t>(OUT_N);
+  return encode_2d_u8(&m->rhs, rb, fn, token_dim, static_cast<uint64_t>(srm), PAIR_TOKENS) ==
+             CUDA_SUCCESS &&
+         encode_2d_u8(&m->lhs, lb, fm, token_dim, static_cast<uint64_t>(slm), PAIR_TOKENS) ==
+             CUDA_SUCCESS &&
+         encode_2d_u8(&m->rhs32, rb, fn, token_dim, static_cast<uint64_t>(srm), 32) ==
+             CUDA_SUCCESS &&
+         encode_2d_u8(&m->lhs32, lb, fm, token_dim, static_cast<uint64_t>(slm), 32) ==
+             CUDA_SUCCESS &&
+         encode_narrow(&m->lhs_n, &m->lhs32_n, lb, OUT_M, token_dim, slm, PAIR_TOKENS,
+                       m->bw_lhs) == CUDA_SUCCESS &&
+         encode_narrow(&m->rhs_n, &m->rhs32_n, rb, OUT_N, token_dim, srm, PAIR_TOKENS,
+                       m->bw_rhs) == CUDA_SUCCESS &&
+         encode_c(&m->c, c, G, OUT_M, OUT_N, scg, scm, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) ==
+             CUDA_SUCCESS;
+}
 
 // Shared with the other entry points of the library (vark_quant.cu): the current device's status
 // block and SM count, set up on first use.
@@ -462,6 +487,41 @@ int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out) {
   *bits_out = words[0];
   if (clear && (e = cudaMemset(blk, 0, 256)) != cudaSuccess) return fail_cuda(e);
   if (clear && (e = cudaDeviceSynchronize()) != cudaSuccess) return fail_cuda(e);
+  return GGEMM_VARK_OK;
+}
+
+int ggemm_vark_read_status_stream(void* status, int clear, uint32_t* words_out, int32_t nwords,
+                                  void* stream) {
+  if (words_out == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  if (nwords < 1 || nwords > 8) return GGEMM_VARK_EINVAL_ARG;
+  if (status != nullptr && !aligned16(status)) return GGEMM_VARK_EINVAL_ARG;
+  uint32_t* blk = static_cast<uint32_t*>(status);
+  if (blk == nullptr) {
+    DeviceState* dev = nullptr;
+    const int rc = get_device(&dev, nullptr);
+    if (rc != GGEMM_VARK_OK) return rc;
+    blk = dev->status;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyAsync(words, blk, sizeof(uint32_t) * nwords, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail_cuda(e);
+  for (int i = 0; i < nwords; ++i) words_out[i] = words[i];
+  // Clear only the words this library writes (0, 1, 4, 5): word 3 holds the test hook.
+  if (clear) {
+    if ((e = cudaMemsetAsync(blk, 0, 2 * sizeof(uint32_t), s)) != cudaSuccess) return fail_cuda(e);
+    if ((e = cudaMemsetAsync(blk + 4, 0, 2 * sizeof(uint32_t), s)) != cudaSuccess)
+      return fail_cuda(e);
+  }
+  return GGEMM_VARK_OK;
+}
+
+int ggemm_vark_device_bytes(int32_t device, uint64_t* bytes_out) {
+  if (bytes_out == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  if (device < 0 || device >= kMaxDevices) return GGEMM_VARK_EINVAL_ARG;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  *bytes_out = g_dev[device].status != nullptr ? kStatusBytes : 0;
   return GGEMM_VARK_OK;
 }
 

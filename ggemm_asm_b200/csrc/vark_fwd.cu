@@ -35,6 +35,13 @@
 //     A TMA store writes a row up to the next 16-byte boundary, so when N is not a multiple of
 //     8 the 32-column chunk that crosses N is written with plain stores as well: nothing past
 //     column N - 1 is touched.
+//   * Unknown M_total (offs_bound, the 14-argument entry point): the A map then ends at the int32
+//     coordinate limit, so every role reads group_offs[G] and no A load touches a row at or past
+//     it. A CTA whose 128-row box would cross it loads the 128 rows that end there instead; its
+//     TMEM lane i then holds token row (group_offs[G] - 128 + i), and the epilogue stores only
+//     the lanes whose rows are this CTA's rows of the expert. Offsets past group_offs[G] are
+//     invalid. The producer records the end of the highest A row any of its loads can read
+//     (status word 4).
 //
 // Warp roles (6 warps, one CTA per SM, 74 pairs on 148 SMs, persistent over a static round-robin
 // of work items by cluster; items ordered expert, token tile, column tile):
@@ -136,6 +143,7 @@ struct Item {
 // the walker created with report = true).
 struct Walker {
   const FwdParams* p;
+  int64_t lim;  // offsets above this are invalid
   bool report;
   int g = -1;
   int64_t base = 0;   // items before expert g
@@ -148,7 +156,7 @@ struct Walker {
     count = 0;
     if (g >= p->G) return;
     const int64_t a = __ldg(p->group_offs + g), b = __ldg(p->group_offs + g + 1);
-    if (a < 0 || b < a || b > p->token_limit || b - a > INT32_MAX) {
+    if (a < 0 || b < a || b > lim || b - a > INT32_MAX) {
       if (report && p->status != nullptr) atomicOr(p->status, GGEMM_VARK_DEV_BAD_OFFS);
       tokens = 0;
       return;
@@ -176,6 +184,21 @@ struct Walker {
     return true;
   }
 };
+
+// Token rows [0, lim) hold valid offsets and, with offs_bound, bound every A load.
+__device__ __forceinline__ int64_t token_rows_limit(const FwdParams& p) {
+  if (!p.offs_bound) return p.token_limit;
+  const int64_t e = __ldg(p.group_offs + p.G);
+  return e < 0 ? 0 : (e < p.token_limit ? e : p.token_limit);
+}
+
+// First A row of CTA `rank`'s box for item t: its own rows (off_g + m0 + 128 rank), or, with
+// M_total unknown and a box that would cross lim, the 128 rows that end at lim.
+__device__ __forceinline__ int64_t a_box_row(const FwdParams& p, int64_t lim, const Item& t,
+                                             uint32_t rank) {
+  const int64_t ya = t.lo + t.m0 + 128 * static_cast<int64_t>(rank);
+  return (p.offs_bound && ya + 128 > lim) ? lim - 128 : ya;
+}
 
 // Shared-memory descriptor offsets of MMA ks (K step of 32) inside a stage, in descriptor units
 // (16 bytes): A and K-major B advance 32 bytes inside a 128-byte box and then jump to the next
@@ -237,6 +260,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 p.status, p.timeout_ns};
   const int64_t cluster = cluster_id_x();
   const int64_t nclusters = num_clusters_x();
+  const int64_t lim = token_rows_limit(p);
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) =======================================
@@ -246,13 +270,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                    GGEMM_VARK_TEST_STALL_MAGIC;
     uint32_t stage = 0, phase = 0;
     bool ok = true;
-    Walker w{&p, false};
+    int64_t rows_end = 0;  // end of the highest A row a load can read (TMA clips at token_limit)
+    Walker w{&p, lim, false};
     Item t;
     const int nkb = (p.K + TK - 1) / TK;
     for (int64_t item = cluster; ok && w.seek(item, &t); item += nclusters) {
-      // Token rows of this CTA's half of the tile, as rows of the whole A (off_g + m0 + 128r;
-      // below the token coordinate limit, so it fits the TMA's int32 coordinate).
-      const int32_t ya = static_cast<int32_t>(t.lo) + t.m0 + 128 * static_cast<int32_t>(rank);
+      // Token rows of this CTA's half of the tile, as rows of the whole A (off_g + m0 + 128r,
+      // or moved back to end at group_offs[G]; below the token coordinate limit, so it fits the
+      // TMA's int32 coordinate).
+      const int32_t ya = static_cast<int32_t>(a_box_row(p, lim, t, rank));
+      if (lane == 0) {
+        const int64_t e = static_cast<int64_t>(ya) + 128;
+        rows_end = e > rows_end ? (e < p.token_limit ? e : p.token_limit) : rows_end;
+      }
       const int32_t yb = t.n0 + (t.ncols >> 1) * static_cast<int32_t>(rank);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!warp_wait(ctl, bar_empty + 8 * stage, phase ^ 1u, 0x100u | stage)) {
@@ -283,6 +313,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    if (lane == 0 && p.status != nullptr) atomicMax(p.status + 4, static_cast<uint32_t>(rows_end));
     if (lane == 0) {
       for (int s = 0; s < ST; ++s) {
         const uint64_t t0 = globaltimer_ns();
@@ -301,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const uint32_t idesc0 = idesc_f8f6f4(static_cast<uint32_t>(p.a_fmt), /*B e4m3*/ 0,
                                            /*A K-major*/ 0, BMN ? 1u : 0u, TILE_M, 0);
       const int nkb = (p.K + TK - 1) / TK;
-      Walker w{&p, false};
+      Walker w{&p, lim, false};
       Item t;
       for (int64_t item = cluster; ok && w.seek(item, &t); item += nclusters) {
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
@@ -366,21 +397,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t epi_sh = base + OFF_EPI + (warp - EPI_WARP0) * 2 * EPI_BUF_BYTES;
     const uint32_t leader_tempty = mapa_shared(bar_tempty, 0);
     uint32_t acc = 0, acc_phase = 0, nstore = 0;
-    Walker w{&p, leader && warp == EPI_WARP0 && lane == 0};
+    Walker w{&p, lim, leader && warp == EPI_WARP0 && lane == 0};
     Item t;
     for (int64_t item = cluster; w.seek(item, &t); item += nclusters) {
       const float scale = __ldg(p.a_scale + static_cast<int64_t>(t.g) * p.scale_stride) *
                           __ldg(p.b_scale + static_cast<int64_t>(t.g) * p.scale_stride);
       if (!warp_wait(ctl, bar_tfull + 8 * acc, acc_phase, 0x400u | acc)) break;
       tc_fence_after_sync();
-      const int row0 = t.m0 + 128 * static_cast<int>(rank) + 32 * quarter;  // within the expert
-      if (row0 < t.tokens) {
+      // Expert row of this warp's lane 0: TMEM lane i holds A row (box row + i). This CTA's
+      // own rows of the expert start at m0 + 128 rank; a box moved back (M_total unknown) starts
+      // `shift` rows before them, and its lanes below the CTA's rows are not stored.
+      const int own0 = t.m0 + 128 * static_cast<int>(rank);
+      const int shift = static_cast<int>(t.lo + own0 - a_box_row(p, lim, t, rank));
+      const int row0 = own0 - shift + 32 * quarter;
+      const int lane_lo = max(0, own0 - row0);
+      const int lane_hi = min(EPI_ROWS, t.tokens - row0);
+      if (lane_lo < lane_hi) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
         // 32-column chunks up to the last real column (the store clips columns >= N).
         const int nchunks = (min(t.ncols, p.N - t.n0) + EPI_COLS - 1) / EPI_COLS;
-        // This warp's rows of the expert: all 32, or the expert's ragged last rows.
-        const int live_rows = min(EPI_ROWS, t.tokens - row0);
-        const int32_t crow0 = static_cast<int32_t>(t.lo) + row0;  // as a row of C
+        // This warp's rows of the expert: all 32, or a ragged range of lanes.
+        const bool whole = lane_lo == 0 && lane_hi == EPI_ROWS;
+        const int32_t crow0 = static_cast<int32_t>(t.lo + row0);  // lane 0 as a row of C
         // Lane = token row; a chunk is 32 consecutive columns. Eight of them -> four bf16 pairs.
         auto pack = [&](const uint32_t (&r)[32], int q, uint32_t (&v)[4]) {
 #pragma unroll
@@ -395,11 +433,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const int col0 = t.n0 + c * EPI_COLS;
           // A TMA store writes each row up to the next 16-byte boundary, so the chunk that
           // crosses an N that is not a multiple of 8 goes the plain way too.
-          if (live_rows < EPI_ROWS || ((p.N & 7) != 0 && col0 + EPI_COLS > p.N)) {
-            // The expert's last rows (or the last chunk of a ragged N): each live lane writes
-            // its row's 32 columns (clipped to N) as 16-byte pieces; C rows are 16-byte aligned
-            // (the row pitch is a multiple of 8 elements) and col0 is a multiple of 32.
-            if (lane < live_rows) {
+          if (!whole || ((p.N & 7) != 0 && col0 + EPI_COLS > p.N)) {
+            // The expert's last rows, the live lanes of a box moved back, or the last chunk of
+            // a ragged N: each live lane writes its row's 32 columns (clipped to N) as 16-byte
+            // pieces; C rows are 16-byte aligned (the row pitch is a multiple of 8 elements) and
+            // col0 is a multiple of 32.
+            if (lane >= lane_lo && lane < lane_hi) {
               const int ncv = min(EPI_COLS, p.N - col0);
               uint16_t* const dst = p.c + static_cast<int64_t>(crow0 + lane) * p.stride_cm + col0;
 #pragma unroll

@@ -3,6 +3,7 @@
 
 #include <cstdint>
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace vark {
@@ -61,6 +62,11 @@ struct TcParams {
   int64_t stride_cm;
   int32_t bw_lhs;        // pair kernel: width in bytes (32 or 64) of the narrow LHS maps, 0: none
   int32_t bw_rhs;        // pair kernel: the same for the narrow RHS maps
+  // 1 when the caller did not state m_total (the 14-argument drop-in): the kernel reads
+  // group_offs[G] and no load touches a token row at or past it (boxes that would cross it are
+  // moved to end there), and offsets past it are invalid. 0: the maps end at token_limit and TMA
+  // clips boxes there.
+  int32_t offs_bound;
 };
 
 // Dynamic shared memory the tcgen05 kernel needs (bytes, including alignment slack).
@@ -83,6 +89,7 @@ struct SimtParams {
   int64_t stride_lhs_m, stride_rhs_m, stride_cg, stride_cm, stride_cn;
   int64_t token_limit;
   uint32_t* status;
+  int32_t offs_bound;  // as TcParams::offs_bound: offsets past group_offs[G] are invalid
 };
 
 cudaError_t simt_launch(const SimtParams& p, cudaStream_t stream);
@@ -102,12 +109,25 @@ size_t tc2_smem_bytes();
 // transposed last column tile (B = RHS).
 // Narrow width for a last tile of MMA N = n: 32 or 64 bytes when N / 2 fits, else 0.
 inline int32_t pair_narrow_width(int32_t n) { return n <= 64 ? 32 : (n <= 128 ? 64 : 0); }
-cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
-                       const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
-                       const CUtensorMap& map_lhs_n, const CUtensorMap& map_lhs32_n,
-                       const CUtensorMap& map_rhs_n, const CUtensorMap& map_rhs32_n,
-                       const CUtensorMap& map_c, const TcParams& p, int grid,
-                       cudaStream_t stream);
+struct PairMaps {
+  CUtensorMap lhs, rhs, lhs32, rhs32, lhs_n, lhs32_n, rhs_n, rhs32_n;
+  CUtensorMap c;     // C as {OUT_N, OUT_M, G} bf16, box {32, 32, 1}, 64-byte swizzle
+  int32_t bw_lhs;    // narrow width of lhs_n / lhs32_n (TcParams::bw_lhs)
+  int32_t bw_rhs;    // the same for rhs_n / rhs32_n
+};
+cudaError_t tc2_launch(const PairMaps& maps, const TcParams& p, int grid, cudaStream_t stream);
+
+// The driver's cuTensorMapEncodeTiled, resolved once per process (vark_capi.cu); nullptr if the
+// driver lacks it. Resolving it touches no device memory.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// Every map of one pair-kernel launch (vark_capi.cu), shared by all entry points that launch it:
+// operands with `token_dim` rows (row pitches slm / srm bytes), C with element strides scg / scm.
+// A NULL operand (a call without tokens) is mapped onto c, which is then never loaded through.
+// False if the driver rejects a map.
+bool encode_pair_maps(PairMaps* m, const void* lhs, const void* rhs, void* c, int32_t G,
+                      int32_t OUT_M, int32_t OUT_N, int32_t slm, int32_t srm, int32_t scg,
+                      int32_t scm, uint64_t token_dim);
 cudaError_t tc2_set_attributes();
 
 // Fixed-K grouped GEMM (vark_fwd.cu): C[t, :] = sA * sB_g * A[t, :] . B[g]^T for the tokens t of
@@ -129,6 +149,7 @@ struct FwdParams {
   uint64_t timeout_ns;
   uint16_t* c;            // C base (bf16 bits); row pitch in elements (a multiple of 8)
   int64_t stride_cm;
+  int32_t offs_bound;     // as TcParams::offs_bound, for the rows of A
 };
 size_t fwd2_smem_bytes();
 cudaError_t fwd2_launch(const CUtensorMap& map_a, const CUtensorMap& map_b,

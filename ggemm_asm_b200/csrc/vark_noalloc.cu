@@ -42,7 +42,6 @@ struct Device {
 
 std::mutex g_mu;
 Device g_devs[kMaxDevices];
-PFN_cuTensorMapEncodeTiled_v12000 g_enc = nullptr;
 
 // Once per device, with that device current: resolve the scratch array's device address and
 // the kernel attributes. Nothing here allocates.
@@ -73,17 +72,8 @@ int setup(Device** out) {
       cudaGetLastError();
       return GGEMM_VARK_ECUDA;
     }
-    if (g_enc == nullptr) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q;
-      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-              cudaSuccess ||
-          q != cudaDriverEntryPointSuccess || fn == nullptr) {
-        cudaGetLastError();
-        return GGEMM_VARK_ECUDA;
-      }
-      g_enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+    // The same encoder and map layout as the regular entry points (vark_capi.cu).
+    if (vark::tensor_map_encoder() == nullptr) return GGEMM_VARK_ECUDA;
     d.scratch = static_cast<uint8_t*>(ptr);
     d.ready = true;
   }
@@ -92,32 +82,6 @@ int setup(Device** out) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-CUresult encode_operand(CUtensorMap* m, const void* base, int32_t features, uint64_t tokens,
-                        int32_t pitch, uint32_t box_tokens = vark::PAIR_TOKENS,
-                        uint32_t box_inner = 128,
-                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(features), tokens};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[2] = {box_inner, box_tokens};
-  const cuuint32_t estr[2] = {1, 1};
-  return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-}
-
-CUresult encode_out(CUtensorMap* m, void* c, int32_t G, int32_t OUT_M, int32_t OUT_N,
-                    int32_t scg, int32_t scm) {
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OUT_N), static_cast<cuuint64_t>(OUT_M),
-                              static_cast<cuuint64_t>(G)};
-  const cuuint64_t strides[2] = {2ull * static_cast<cuuint64_t>(scm),
-                                 2ull * static_cast<cuuint64_t>(scg)};
-  const cuuint32_t box[3] = {32, 32, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return g_enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, c, dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-}
 
 }  // namespace
 
@@ -129,11 +93,12 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
                                             int32_t stride_cm, int32_t stride_cn,
                                             int64_t m_total, int32_t scale_stride,
                                             void* status, void* stream) {
-  // Same argument rules as ggemm_vark_fp8_wgrad_ex, restricted to layouts the tensor-core
-  // kernel takes (this entry point has no CUDA-core fallback).
+  // Same argument rules as ggemm_vark_fp8_wgrad_ex (lhs and rhs may be NULL only with
+  // m_total == 0), restricted to layouts the tensor-core kernel takes (this entry point has no
+  // CUDA-core fallback).
   if (c == nullptr || lhs_scale == nullptr || rhs_scale == nullptr || group_offs == nullptr)
     return GGEMM_VARK_EINVAL_PTR;
-  if (lhs == nullptr || rhs == nullptr) return GGEMM_VARK_EINVAL_PTR;
+  if (m_total != 0 && (lhs == nullptr || rhs == nullptr)) return GGEMM_VARK_EINVAL_PTR;
   if (G < 0 || OUT_M <= 0 || OUT_N <= 0) return GGEMM_VARK_EINVAL_SHAPE;
   if (stride_lhs_m < OUT_M || stride_rhs_m < OUT_N || stride_cn <= 0 || stride_cm <= 0 ||
       stride_cg <= 0)
@@ -158,36 +123,15 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   const int64_t token_limit =
       m_total >= 0 ? (m_total < kTokenCoordLimit ? m_total : kTokenCoordLimit) : kTokenCoordLimit;
   const uint64_t token_dim = token_limit > 0 ? static_cast<uint64_t>(token_limit) : 1u;
-  CUtensorMap map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n,
-      map_rhs32_n, map_c;
-  // Narrow B boxes for the last row tile (LHS) and the transposed last column tile (RHS).
-  const int32_t last_rows = OUT_M - vark::PAIR_ROWS_MAX * (row_tiles - 1);
-  const int32_t last_cols = OUT_N - vark::PAIR_COLS * (col_tiles - 1);
-  const int32_t bw_lhs = vark::pair_narrow_width((last_rows + 31) & ~31);
-  const int32_t bw_rhs =
-      last_cols < vark::PAIR_COLS ? vark::pair_narrow_width((last_cols + 31) & ~31) : 0;
-  const uint32_t wl = bw_lhs == 64 ? 64u : 32u, wr = bw_rhs == 64 ? 64u : 32u;
-  const CUtensorMapSwizzle swl = wl == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  const CUtensorMapSwizzle swr = wr == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  if (encode_operand(&map_lhs, lhs, OUT_M, token_dim, stride_lhs_m) != CUDA_SUCCESS ||
-      encode_operand(&map_rhs, rhs, OUT_N, token_dim, stride_rhs_m) != CUDA_SUCCESS ||
-      encode_operand(&map_lhs32, lhs, OUT_M, token_dim, stride_lhs_m, 32) != CUDA_SUCCESS ||
-      encode_operand(&map_rhs32, rhs, OUT_N, token_dim, stride_rhs_m, 32) != CUDA_SUCCESS ||
-      encode_operand(&map_lhs_n, lhs, OUT_M, token_dim, stride_lhs_m, vark::PAIR_TOKENS, wl,
-                     swl) != CUDA_SUCCESS ||
-      encode_operand(&map_lhs32_n, lhs, OUT_M, token_dim, stride_lhs_m, 32, wl, swl) !=
-          CUDA_SUCCESS ||
-      encode_operand(&map_rhs_n, rhs, OUT_N, token_dim, stride_rhs_m, vark::PAIR_TOKENS, wr,
-                     swr) != CUDA_SUCCESS ||
-      encode_operand(&map_rhs32_n, rhs, OUT_N, token_dim, stride_rhs_m, 32, wr, swr) !=
-          CUDA_SUCCESS ||
-      encode_out(&map_c, c, G, OUT_M, OUT_N, stride_cg, stride_cm) != CUDA_SUCCESS)
+  vark::PairMaps maps;
+  if (!vark::encode_pair_maps(&maps, lhs, rhs, c, G, OUT_M, OUT_N, stride_lhs_m, stride_rhs_m,
+                              stride_cg, stride_cm, token_dim))
     return GGEMM_VARK_ELAYOUT;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint32_t* st = status != nullptr ? static_cast<uint32_t*>(status)
                                    : reinterpret_cast<uint32_t*>(d->scratch);
-  if (status == nullptr && cudaMemsetAsync(d->scratch, 0, 16, s) != cudaSuccess) {
+  if (status == nullptr && cudaMemsetAsync(d->scratch, 0, 32, s) != cudaSuccess) {
     cudaGetLastError();
     return GGEMM_VARK_ECUDA;
   }
@@ -208,12 +152,11 @@ extern "C" int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs, vo
   tp.c = static_cast<uint16_t*>(c);
   tp.stride_cg = stride_cg;
   tp.stride_cm = stride_cm;
-  tp.bw_lhs = bw_lhs;
-  tp.bw_rhs = bw_rhs;
+  tp.bw_lhs = maps.bw_lhs;
+  tp.bw_rhs = maps.bw_rhs;
+  tp.offs_bound = m_total < 0 ? 1 : 0;
   const int64_t clusters = items < d->sm_count / 2 ? items : d->sm_count / 2;
-  const cudaError_t e =
-      vark::tc2_launch(map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n,
-                       map_rhs32_n, map_c, tp, static_cast<int>(2 * clusters), s);
+  const cudaError_t e = vark::tc2_launch(maps, tp, static_cast<int>(2 * clusters), s);
   if (e != cudaSuccess) return GGEMM_VARK_ECUDA;
   return GGEMM_VARK_OK;
 }

@@ -33,7 +33,9 @@ __global__ void __launch_bounds__(256) vark_simt_kernel(const SimtParams p) {
 
   int64_t lo = p.group_offs[g];
   int64_t hi = p.group_offs[g + 1];
-  if (lo < 0 || hi < lo || hi > p.token_limit) {
+  // Without m_total, group_offs[G] is the token count (rows are read only inside groups).
+  const int64_t lim = p.offs_bound ? min(p.group_offs[p.G], p.token_limit) : p.token_limit;
+  if (lo < 0 || hi < lo || hi > lim) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && p.status != nullptr)
       atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
     lo = hi = 0;

@@ -30,6 +30,13 @@
 // makes the writes visible to the tensor core (proxy fence) and then releases the stage to the
 // MMA warp. Empty groups skip the pipeline: the epilogue TMA-stores zeros for them.
 //
+// Unknown M_total (offs_bound): every role reads group_offs[G] and no load touches a token row at
+// or past it. A group's last block whose box would cross it is loaded as the 128 tokens that end
+// with the group; its tokens then occupy the last ceil(rem / 32) K steps of the stage, the first
+// of them starting with (32 - rem % 32) % 32 earlier tokens, which the producer zeroes. Offsets
+// past group_offs[G] are invalid. The producer records the end of the highest token row any of
+// its loads can read (status words 4 = LHS, 5 = RHS).
+//
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA sets the abort
 // flag and GGEMM_VARK_DEV_TIMEOUT in the status block, every role leaves its loop, in-flight
 // TMA loads and MMAs are drained with bounded waits, TMEM is freed and the CTA returns.
@@ -116,7 +123,21 @@ struct TileInfo {
   int64_t end;     // off_{g+1}
 };
 
-__device__ __forceinline__ TileInfo decode_tile(const TcParams& p, int tile, bool report) {
+// Token rows [0, lim) hold valid offsets and, with offs_bound, bound every load.
+__device__ __forceinline__ int64_t token_rows_limit(const TcParams& p) {
+  if (!p.offs_bound) return p.token_limit;
+  const int64_t e = __ldg(p.group_offs + p.G);
+  return e < 0 ? 0 : (e < p.token_limit ? e : p.token_limit);
+}
+
+// First K step of a group's last block that holds its tokens: nonzero when the block was moved
+// back to end with the group (M_total unknown and the box would cross group_offs[G]).
+__device__ __forceinline__ int last_block_slot0(bool bounded, int64_t y, int rem, int64_t lim) {
+  return (bounded && y + TILE_TOKENS > lim) ? (TILE_TOKENS - rem) >> 5 : 0;
+}
+
+__device__ __forceinline__ TileInfo decode_tile(const TcParams& p, int64_t lim, int tile,
+                                                bool report) {
   const int per_group = p.row_tiles * p.col_tiles;
   TileInfo t;
   t.g = tile / per_group;
@@ -125,7 +146,7 @@ __device__ __forceinline__ TileInfo decode_tile(const TcParams& p, int tile, boo
   t.col0 = (r / p.row_tiles) * TILE_COLS;
   const int64_t lo = __ldg(p.group_offs + t.g);
   const int64_t hi = __ldg(p.group_offs + t.g + 1);
-  if (lo < 0 || hi < lo || hi > p.token_limit) {
+  if (lo < 0 || hi < lo || hi > lim) {
     if (report && p.status != nullptr) atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
     t.tokens = 0;
     t.end = 0;
@@ -191,6 +212,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const Ctl ctl{abort_flag, p.status, p.timeout_ns};
   const int num_tiles = p.G * p.row_tiles * p.col_tiles;
+  const int64_t lim = token_rows_limit(p);
+  const bool bounded = p.offs_bound != 0;
 
   if (warp == 0) {
     // ======================= TMA producer (lane 0 issues; the warp stays converged) ==========
@@ -202,8 +225,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t stage = 0, phase = 0, zphase = 0;
     uint32_t used_mask = 0, parity_mask = 0;  // per stage: issued at least once / last parity
     bool ok = true, zpending = false;
+    int64_t rows_end = 0;  // end of the highest token row a load can read (TMA clips at token_limit)
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const TileInfo t = decode_tile(p, tile, false);
+      const TileInfo t = decode_tile(p, lim, tile, false);
       if (t.tokens == 0) continue;
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
       const int rem = t.tokens - TILE_TOKENS * (nkb - 1);  // the group's tokens in its last block
@@ -217,7 +241,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t fb = bar_full + 8 * stage;
         const uint32_t rhs_dst = base + OFF_RHS + stage * RHS_STAGE_BYTES;
         const uint32_t lhs_dst = base + OFF_LHS + stage * LHS_STAGE_BYTES;
-        const int32_t y = lo + TILE_TOKENS * kb;
+        const int64_t y_block = static_cast<int64_t>(lo) + TILE_TOKENS * kb;
+        // M_total unknown and the last block's box would cross group_offs[G]: the block is
+        // moved back so that it ends with the group's rem tokens.
+        const bool back = kb == nkb - 1 && bounded && y_block + TILE_TOKENS > lim;
+        const int32_t y = static_cast<int32_t>(back ? y_block + rem - TILE_TOKENS : y_block);
         // A group's last block that ends inside a K step (32 tokens): the MMA warp multiplies
         // that step, so its rows [rem, ceil32(rem)) must be zero. The block lands on bar_zfill
         // instead and those rows are zeroed before the stage is released to the MMA warp. (The
@@ -228,6 +256,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t lb = last_partial ? bar_zfill : fb;
           if (lane == 0) {
             mbar_arrive_expect_tx(lb, STAGE_TX_BYTES);
+            const int64_t e = static_cast<int64_t>(y) + TILE_TOKENS;
+            rows_end = e > rows_end ? (e < p.token_limit ? e : p.token_limit) : rows_end;
             tma_load_2d_hint(rhs_dst, &map_rhs, lb, t.col0, y, policy);
 #pragma unroll
             for (int b = 0; b < LHS_BOXES; ++b)
@@ -242,13 +272,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             zpending = false;
             zphase ^= 1u;
-            // Whole 128-byte token rows, so the 128-byte swizzle does not matter.
-            const uint32_t keep = static_cast<uint32_t>(rem) * 128u;
-            const uint32_t zbytes = static_cast<uint32_t>((rem + 31) & ~31) * 128u - keep;
-            smem_zero_warp(rhs_dst + keep, zbytes, lane);
+            // Whole 128-byte token rows, so the 128-byte swizzle does not matter. A block moved
+            // back zeroes the earlier tokens in front of its first step instead.
+            const uint32_t z0 = back ? static_cast<uint32_t>((TILE_TOKENS - rem) & ~31) * 128u
+                                     : static_cast<uint32_t>(rem) * 128u;
+            const uint32_t zbytes = back ? static_cast<uint32_t>(TILE_TOKENS - rem) * 128u - z0
+                                         : static_cast<uint32_t>((rem + 31) & ~31) * 128u - z0;
+            smem_zero_warp(rhs_dst + z0, zbytes, lane);
 #pragma unroll
             for (int b = 0; b < LHS_BOXES; ++b)
-              smem_zero_warp(lhs_dst + b * LHS_BOX_BYTES + keep, zbytes, lane);
+              smem_zero_warp(lhs_dst + b * LHS_BOX_BYTES + z0, zbytes, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(fb);
@@ -263,6 +296,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           phase ^= 1u;
         }
       }
+    }
+    if (lane == 0 && p.status != nullptr) {
+      atomicMax(p.status + 4, static_cast<uint32_t>(rows_end));  // LHS and RHS boxes alike
+      atomicMax(p.status + 5, static_cast<uint32_t>(rows_end));
     }
     // Drain: every issued load must have landed before the CTA may exit. On the normal path
     // they all have (the MMA warp consumed them); after an abort the wait is bounded.
@@ -289,10 +326,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc = 0, acc_phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const TileInfo t = decode_tile(p, tile, false);
+      const TileInfo t = decode_tile(p, lim, tile, false);
       if (t.tokens == 0) continue;
       const int nkb = (t.tokens + TILE_TOKENS - 1) / TILE_TOKENS;
-      const int last_steps = (t.tokens - TILE_TOKENS * (nkb - 1) + 31) >> 5;  // of the last block
+      const int rem = t.tokens - TILE_TOKENS * (nkb - 1);
+      const int last_steps = (rem + 31) >> 5;  // of the last block
+      const int64_t lo = t.end - t.tokens;
       if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
       tc_fence_after_sync();
       const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE_COLS;
@@ -313,10 +352,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
             }
           } else {  // the group's last block: only the K steps that hold its tokens
-            for (int ks = 0; ks < last_steps; ++ks) {
+            const int ks0 = last_block_slot0(bounded, lo + TILE_TOKENS * kb, rem, lim);
+            for (int ks = ks0; ks < ks0 + last_steps; ++ks) {
               const uint64_t adesc = smem_desc_sw128(a_stage + ks * 4096u, RHS_STAGE_BYTES, 1024u);
               const uint64_t bdesc = smem_desc_sw128(b_stage + ks * 4096u, LHS_BOX_BYTES, 1024u);
-              mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+              mma_f8f6f4(d_tmem, adesc, bdesc, IDESC, (kb > 0 || ks > ks0) ? 1u : 0u);
             }
           }
           mma_commit(bar_empty + 8 * stage);  // frees the stage once these MMAs finish
@@ -354,7 +394,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc = 0, acc_phase = 0;
     uint32_t nstore = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const TileInfo t = decode_tile(p, tile, quarter == 0 && lane == 0);
+      const TileInfo t = decode_tile(p, lim, tile, quarter == 0 && lane == 0);
       const int xcol = t.col0 + quarter * 32;
       const bool col_live = xcol < p.OUT_N;
       const int rows_here = min(TILE_ROWS, p.OUT_M - t.row0);

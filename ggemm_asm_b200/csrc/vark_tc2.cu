@@ -52,6 +52,17 @@
 // with a cluster-scope acquire, so the zeroing is off the MMA's critical path. Empty groups
 // skip the pipeline and the epilogue stores zeros.
 //
+// Unknown M_total (the 14-argument drop-in). The maps then end at the int32 coordinate limit, so
+// TMA would not clip anything; instead every role reads group_offs[G] once and no load touches a
+// token row at or past it: a group's last block whose box would cross it is loaded shifted back
+// by whole K steps, so that it ends with the block's last whole step (the MMA warp starts that
+// many steps into the stage), and a tail chunk that would cross it is loaded as the 32 tokens
+// that end with the group, its first 32 - ragged rows (the group's earlier tokens, already
+// multiplied) being the ones the producer zeroes. Offsets past group_offs[G] are invalid. With
+// M_total known the maps end there and TMA clips boxes without reading memory, so nothing moves.
+// The producer records, per operand, the end of the highest token row any of its loads can read
+// (status words 4 = LHS, 5 = RHS).
+//
 // Every mbarrier wait is bounded (TcParams::timeout_ns). On expiry the CTA flags
 // GGEMM_VARK_DEV_TIMEOUT, sets the abort flag of both CTAs of the pair, every role leaves its
 // loop, in-flight loads and MMAs are drained with bounded waits, and the pair meets at a
@@ -162,7 +173,15 @@ struct Item {
   uint32_t bw;     // B bytes per token row in shared memory: 128, or 64 / 32 (narrow maps)
 };
 
-__device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool report) {
+// Token rows [0, lim) hold valid offsets and, with offs_bound, bound every load.
+__device__ __forceinline__ int64_t token_rows_limit(const TcParams& p) {
+  if (!p.offs_bound) return p.token_limit;
+  const int64_t e = __ldg(p.group_offs + p.G);
+  return e < 0 ? 0 : (e < p.token_limit ? e : p.token_limit);
+}
+
+__device__ __forceinline__ Item decode_item(const TcParams& p, int64_t lim, int item,
+                                            bool report) {
   const int per_group = p.row_tiles * p.col_tiles;
   Item t;
   t.g = item / per_group;
@@ -177,7 +196,7 @@ __device__ __forceinline__ Item decode_item(const TcParams& p, int item, bool re
   t.bw = (nw > 0 && b_half <= nw) ? static_cast<uint32_t>(nw) : 128u;
   const int64_t lo = __ldg(p.group_offs + t.g);
   const int64_t hi = __ldg(p.group_offs + t.g + 1);
-  if (lo < 0 || hi < lo || hi > p.token_limit) {
+  if (lo < 0 || hi < lo || hi > lim) {
     if (report && p.status != nullptr) atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
     t.tokens = 0;
     t.end = 0;
@@ -259,6 +278,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const Ctl ctl{abort_flag, mapa_shared(smem_u32(const_cast<int*>(abort_flag)), rank ^ 1u),
                 p.status, p.timeout_ns};
   const int num_items = p.G * p.row_tiles * p.col_tiles;
+  const int64_t lim = token_rows_limit(p);
+  const bool bounded = p.offs_bound != 0;
   const int cluster = static_cast<int>(cluster_id_x());
   const int nclusters = static_cast<int>(num_clusters_x());
 
@@ -275,24 +296,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // finished at the producer's next stop, when the tail has usually landed; the MMA warp only
     // needs the tail after the item's whole K steps.
     int ztail = -1;
-    uint32_t zkeep = 0, zkeep_b = 0, zend_b = TAIL_BYTES;  // A rows are 128 B, B rows 128 or 32
+    // Byte ranges of the pending tail to zero: A rows are 128 B, B rows 128, 64 or 32 B.
+    uint32_t za0 = 0, za1 = 0, zb0 = 0, zb1 = 0;
+    // End of the highest token row a load of each operand can read (TMA clips at token_limit).
+    int64_t rows_lhs = 0, rows_rhs = 0;
+    auto note_rows = [&](bool a_is_lhs, int64_t end_a, int64_t end_b) {
+      const int64_t ea = end_a < p.token_limit ? end_a : p.token_limit;
+      const int64_t eb = end_b < p.token_limit ? end_b : p.token_limit;
+      if (a_is_lhs) {
+        rows_lhs = ea > rows_lhs ? ea : rows_lhs;
+        rows_rhs = eb > rows_rhs ? eb : rows_rhs;
+      } else {
+        rows_rhs = ea > rows_rhs ? ea : rows_rhs;
+        rows_lhs = eb > rows_lhs ? eb : rows_lhs;
+      }
+    };
     auto finish_zfill = [&]() -> bool {
       if (ztail < 0) return true;
       if (!warp_wait(ctl, bar_zfill, zphase, 0x600u)) return false;
       zphase ^= 1u;
       const uint32_t ta = base + OFF_TAIL + static_cast<uint32_t>(ztail) * 2u * TAIL_BYTES;
-      smem_zero_warp(ta + zkeep, TAIL_BYTES - zkeep, lane);
-      smem_zero_warp(ta + TAIL_BYTES + zkeep_b, zend_b - zkeep_b, lane);
+      smem_zero_warp(ta + za0, za1 - za0, lane);
+      smem_zero_warp(ta + TAIL_BYTES + zb0, zb1 - zb0, lane);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive_release_cluster(mapa_shared(bar_tail_full + 8 * ztail, 0));
       ztail = -1;
       return true;
     };
-    Item nxt = decode_item(p, cluster, false);
+    Item nxt = decode_item(p, lim, cluster, false);
     for (int item = cluster; item < num_items && ok; item += nclusters) {
       const Item t = nxt;  // decoded one item ahead: the offsets' load latency is hidden
-      if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
+      if (item + nclusters < num_items) nxt = decode_item(p, lim, item + nclusters, false);
       if (t.tokens == 0) continue;
       const int steps = t.tokens >> 5;                 // whole 32-token K steps
       const int ragged = t.tokens & 31;                // tokens of the tail step
@@ -309,7 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // The tail: one 32-token chunk from the group's last whole step on, into a tail buffer
         // (two, used in turn), loaded first so that its zeroing is long done when the MMA warp
         // reaches it. Rows [ragged, 32) of it are not the group's (another group's tokens, or
-        // TMA zero fill past M_total).
+        // TMA zero fill past M_total); in a chunk moved back, rows [0, 32 - ragged) are not.
         const uint32_t tb = ntail & 1u;
         const uint32_t tpar = ((ntail >> 1) & 1u) ^ 1u;
         if (!finish_zfill() || !warp_wait(ctl, bar_tail_empty + 8 * tb, tpar, 0x700u | tb)) {
@@ -318,7 +353,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         ++ntail;
         const uint32_t ta = base + OFF_TAIL + tb * 2u * TAIL_BYTES;
-        const int32_t y = lo + 32 * steps;
+        const int32_t y0 = lo + 32 * steps;
+        // Unknown M_total and a chunk that would cross group_offs[G]: the 32 tokens ending with
+        // the group instead, whose first 32 - ragged rows are zeroed (see the file comment).
+        const bool back = bounded && static_cast<int64_t>(y0) + 32 > lim;
+        const int32_t y = back ? y0 + ragged - 32 : y0;
         const bool nb = t.bw != 128u;
         const uint32_t tail_b = t.bw * 32u;
         if (lane == 0) {
@@ -328,11 +367,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                            t.edge ? (nb ? &map_rhs32_n : &map_rhs32)
                                   : (nb ? &map_lhs32_n : &map_lhs32),
                            bar_zfill, xb, y, policy);
+          note_rows(t.edge, static_cast<int64_t>(y) + 32, static_cast<int64_t>(y) + 32);
         }
         ztail = static_cast<int>(tb);
-        zkeep = static_cast<uint32_t>(ragged) * 128u;
-        zkeep_b = static_cast<uint32_t>(ragged) * t.bw;
-        zend_b = tail_b;
+        const uint32_t keep = static_cast<uint32_t>(back ? 32 - ragged : ragged);
+        za0 = back ? 0u : keep * 128u;
+        za1 = back ? keep * 128u : TAIL_BYTES;
+        zb0 = back ? 0u : keep * t.bw;
+        zb1 = back ? keep * t.bw : tail_b;
       }
       const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
       const bool nb = t.bw != 128u;
@@ -348,12 +390,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         if (lane == 0 && !withhold) {
-          // The last block's rows past the whole steps are loaded but never multiplied.
+          // The last block's rows past the whole steps are loaded but never multiplied. With
+          // M_total unknown, a last block whose box would cross group_offs[G] is moved back by
+          // whole steps so that it ends with its last whole step.
           const uint32_t fb = mapa_shared(bar_full + 8 * stage, 0);  // leader's barrier
-          const int32_t y = lo + TK * kb;
+          int32_t y = lo + TK * kb;
+          if (bounded && static_cast<int64_t>(y) + TK > lim) y += 32 * (steps - SPB * kb) - TK;
           mbar_arrive_expect_tx_cluster(fb, stage_bytes);
           tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, map_a, fb, xa, y, policy);
           tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, map_b, fb, xb, y, policy);
+          note_rows(t.edge, static_cast<int64_t>(y) + TK, static_cast<int64_t>(y) + TK);
         }
         __syncwarp();
         withhold = false;
@@ -364,6 +410,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (ok && !finish_zfill()) ok = false;
+    if (lane == 0 && p.status != nullptr) {
+      atomicMax(p.status + 4, static_cast<uint32_t>(rows_lhs));
+      atomicMax(p.status + 5, static_cast<uint32_t>(rows_rhs));
+    }
     // Loads still in flight are drained through the empty barriers: every stage and tail this
     // producer filled is released by the leader's commit once its MMAs (which waited for the
     // data) finish; a tail still pending after an abort is drained on its own barrier. After an
@@ -400,10 +450,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0, ntail = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
-      Item nxt = decode_item(p, cluster, false);
+      Item nxt = decode_item(p, lim, cluster, false);
       for (int item = cluster; item < num_items && ok; item += nclusters) {
         const Item t = nxt;
-        if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, false);
+        if (item + nclusters < num_items) nxt = decode_item(p, lim, item + nclusters, false);
         if (t.tokens == 0) continue;
         const int steps = t.tokens >> 5;
         const int ragged = t.tokens & 31;
@@ -440,9 +490,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 mma_f8f6f4_pair(d_tmem, a0 + ks * 256u, b0 + ks * b_step, idesc,
                                 (kb > 0 || ks > 0) ? 1u : 0u);
             } else {  // the last block: only its whole steps
-              for (int ks = 0; ks < ks_n; ++ks)
+              // A block the producer moved back (M_total unknown) holds them at its end.
+              const int64_t y = t.end - t.tokens + static_cast<int64_t>(TK) * kb;
+              const int ks0 = (bounded && y + TK > lim) ? SPB - ks_n : 0;
+              for (int ks = ks0; ks < ks0 + ks_n; ++ks)
                 mma_f8f6f4_pair(d_tmem, a0 + ks * 256u, b0 + ks * b_step, idesc,
-                                (kb > 0 || ks > 0) ? 1u : 0u);
+                                (kb > 0 || ks > ks0) ? 1u : 0u);
             }
             mma_commit_pair(bar_empty + 8 * stage, 0x3);  // frees the stage in both CTAs
           }
@@ -504,10 +557,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       return buf;
     };
     const bool reporter = leader && ew == 0 && lane == 0;
-    Item nxt = decode_item(p, cluster, reporter);
+    Item nxt = decode_item(p, lim, cluster, reporter);
     for (int item = cluster; item < num_items; item += nclusters) {
       const Item t = nxt;
-      if (item + nclusters < num_items) nxt = decode_item(p, item + nclusters, reporter);
+      if (item + nclusters < num_items) nxt = decode_item(p, lim, item + nclusters, reporter);
       // This warp's 32 TMEM lanes are 32 C columns starting at xcol (normal items) or 32 C rows
       // starting at row0 (edge items); TMEM column chunk c is 32 C rows (normal) or 32 C
       // columns (edge) of those.
@@ -653,15 +706,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 size_t tc2_smem_bytes() { return SMEM_ALLOC; }
 
-cudaError_t tc2_launch(const CUtensorMap& map_lhs, const CUtensorMap& map_rhs,
-                       const CUtensorMap& map_lhs32, const CUtensorMap& map_rhs32,
-                       const CUtensorMap& map_lhs_n, const CUtensorMap& map_lhs32_n,
-                       const CUtensorMap& map_rhs_n, const CUtensorMap& map_rhs32_n,
-                       const CUtensorMap& map_c, const TcParams& p, int grid,
-                       cudaStream_t stream) {
+cudaError_t tc2_launch(const PairMaps& m, const TcParams& p, int grid, cudaStream_t stream) {
   vark_tc2_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(
-      map_lhs, map_rhs, map_lhs32, map_rhs32, map_lhs_n, map_lhs32_n, map_rhs_n, map_rhs32_n,
-      map_c, p);
+      m.lhs, m.rhs, m.lhs32, m.rhs32, m.lhs_n, m.lhs32_n, m.rhs_n, m.rhs32_n, m.c, p);
   return cudaGetLastError();
 }
 

@@ -31,8 +31,19 @@ def grouped_gemm_fp8_tensorwise(a: torch.Tensor, b: torch.Tensor, a_scale: torch
 
     a_scale / b_scale: float32, both 1 element (tensorwise, as the harness) or both G elements
     (per expert). ``out`` (optional): [M_total, N] bf16 with contiguous rows; rows of every
-    expert are overwritten.
+    expert are overwritten. Called without ``out``, ``status`` or ``timeout_ns`` it runs as the
+    registered operator torch.ops.ggemm.grouped_fp8_fwd (traceable; see ops.py).
     """
+    if out is None and status is None and timeout_ns == 0:
+        from . import ops
+
+        return ops.grouped_fp8_fwd(a, b, a_scale, b_scale, group_offs, bool(trans_b))
+    return _grouped_fwd(a, b, a_scale, b_scale, group_offs, trans_b, out, status, timeout_ns)
+
+
+def _grouped_fwd(a, b, a_scale, b_scale, group_offs, trans_b=True, out=None, status=None,
+                 timeout_ns=0) -> torch.Tensor:
+    """The C-ABI call behind grouped_gemm_fp8_tensorwise and its operator."""
     if a.dtype not in A_FORMATS or b.dtype != torch.float8_e4m3fn:
         raise TypeError(f"expected a float8_e4m3fn/float8_e5m2 and b float8_e4m3fn, got "
                         f"{a.dtype} and {b.dtype}")

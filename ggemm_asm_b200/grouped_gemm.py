@@ -74,7 +74,19 @@ def grouped_gemm_fp8_tensorwise_variable_k(lhs: torch.Tensor, rhs: torch.Tensor,
     with contiguous rows; it is overwritten. ``path`` selects "auto" | "tcgen05" (CTA pairs) |
     "tcgen05_1sm" (single CTA) | "simt".
     ``status``: optional int32 CUDA tensor of >= 64 elements used as the device status block.
+    Called without ``out``, ``path`` or ``status`` it runs as the registered operator
+    torch.ops.ggemm.variable_k_wgrad (traceable; see ops.py).
     """
+    if out is None and path == "auto" and status is None:
+        from . import ops
+
+        return ops.variable_k_wgrad(lhs, rhs, lhs_scale, rhs_scale, group_offs)
+    return _variable_k_wgrad(lhs, rhs, lhs_scale, rhs_scale, group_offs, out, path, status)
+
+
+def _variable_k_wgrad(lhs, rhs, lhs_scale, rhs_scale, group_offs, out=None, path="auto",
+                      status=None) -> torch.Tensor:
+    """The C-ABI call behind grouped_gemm_fp8_tensorwise_variable_k and its operator."""
     G, scale_stride = _check_inputs(lhs, rhs, lhs_scale, rhs_scale, group_offs)
     OUT_M, OUT_N = lhs.shape[1], rhs.shape[1]
     if out is None:

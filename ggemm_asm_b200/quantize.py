@@ -33,7 +33,20 @@ def quantize_fp8(x: torch.Tensor, group_offs: torch.Tensor, fmt: str = "e4m3", *
     out / scales: optional outputs ([tokens, F] fp8 with contiguous rows; fp32 [G] or [1]).
     status / timeout_ns: optional int32 status block (>= 64 elements) and wait limit (ns).
     Rows outside [offs[0], offs[G]) are left as they are in ``out`` (uninitialised if new).
+    Called without ``out``, ``scales``, ``status`` or ``timeout_ns`` it runs as the registered
+    operator torch.ops.ggemm.quantize_fp8 (traceable; see ops.py).
     """
+    if out is None and scales is None and status is None and timeout_ns == 0 and \
+            granularity in ("group", "tensor") and fmt in FORMATS:
+        from . import ops
+
+        return ops.quantize_fp8(x, group_offs, fmt, granularity == "group")
+    return _quantize_fp8(x, group_offs, fmt, granularity, out, scales, status, timeout_ns)
+
+
+def _quantize_fp8(x, group_offs, fmt="e4m3", granularity="group", out=None, scales=None,
+                  status=None, timeout_ns=0) -> tuple[torch.Tensor, torch.Tensor]:
+    """The C-ABI call behind quantize_fp8 and its operator."""
     if fmt not in FORMATS:
         raise ValueError(f"fmt must be one of {sorted(FORMATS)}, got {fmt!r}")
     if granularity not in ("group", "tensor"):

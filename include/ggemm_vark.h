@@ -25,7 +25,12 @@
  *    stream); no host synchronisation and no device-to-host copy of group_offs happens;
  *  - C is always fully overwritten (no accumulate-into-C);
  *  - the return value is 0 on success or a GGEMM_VARK_E* code (nothing is launched on error);
- *  - entry points are safe to call from several host threads on distinct streams.
+ *  - entry points may be called from several host threads on distinct streams. A call given no
+ *    status block records its device-side status in the library's one block for the current
+ *    device, which every such call on that device shares: a bit found there cannot be traced to
+ *    one call. Give each stream its own block (the `status` argument of the _ex entry points)
+ *    to keep them apart. ggemm_vark_read_status synchronises the whole device;
+ *    ggemm_vark_read_status_stream waits for one stream only.
  */
 #ifndef GGEMM_VARK_H_
 #define GGEMM_VARK_H_
@@ -55,8 +60,23 @@ extern "C" {
 #define GGEMM_VARK_ETOO_LARGE         8  /* a size exceeds the documented maximum */
 
 /* ---- device-side status bits (read with ggemm_vark_read_status) -------------------------- */
-#define GGEMM_VARK_DEV_BAD_OFFS   0x1u   /* group_offs not monotone, negative, or past m_total */
+#define GGEMM_VARK_DEV_BAD_OFFS   0x1u   /* group_offs not monotone, negative, or past m_total
+                                            (past group_offs[G] when m_total is not given) */
 #define GGEMM_VARK_DEV_TIMEOUT    0x2u   /* a pipeline wait exceeded its limit; the CTA stopped */
+
+/* ---- status block layout (32-bit words; a caller's block is >= 256 bytes, 16-byte aligned) -
+ *  word 0  GGEMM_VARK_DEV_* bits, or-ed by every launch
+ *  word 1  where a wait expired (GGEMM_VARK_DEV_TIMEOUT), for diagnosis
+ *  word 3  the failure-detection test hook (GGEMM_VARK_TEST_STALL_MAGIC); never written
+ *  word 4  wgrad: the end (exclusive) of the highest LHS token row any load of the tensor-core
+ *          kernels could read, maximum over launches; fixed-K GEMM: the same for A's rows
+ *  word 5  wgrad: the same for RHS
+ * A load past M_total when m_total is given is clipped by the hardware without reading memory,
+ * so words 4 and 5 never exceed m_total; without m_total they never exceed group_offs[G]. */
+#define GGEMM_VARK_STATUS_WORD_BITS      0
+#define GGEMM_VARK_STATUS_WORD_SITE      1
+#define GGEMM_VARK_STATUS_WORD_LHS_ROWS  4
+#define GGEMM_VARK_STATUS_WORD_RHS_ROWS  5
 
 /* ---- test hook for failure detection ------------------------------------------------------
  * If word 3 of a caller-provided status block (ggemm_vark_fp8_wgrad_ex's `status`) holds this
@@ -78,10 +98,12 @@ extern "C" {
  * Replaces the launch in bench.py:364-413 (prepare_variable_k_args / launch_variable_k_kernel)
  * and launcher.cpp:123-168 (KernelArgs + hipModuleLaunchKernel); argument order and meaning are
  * the reference's (README.md:88-95). Per-tensor scales (one fp32 each). The token count
- * M_total is not an argument, exactly as in the reference: group_offs is trusted to lie inside
- * the LHS/RHS allocations. The first call on a device makes the library's one allocation for
- * that device (cudaMalloc of the 4 KiB status block); make the first call before any stream
- * capture.
+ * M_total is not an argument, exactly as in the reference: group_offs[G] is taken as M_total.
+ * No load reads a token row at or past it (the kernel reads group_offs[G] on the device and
+ * moves the boxes that would cross it), so LHS and RHS allocations of exactly group_offs[G] rows
+ * are safe; offsets past group_offs[G] are reported (GGEMM_VARK_DEV_BAD_OFFS) and their groups
+ * written as zeros. The first call on a device makes the library's one allocation for that
+ * device (cudaMalloc of the 4 KiB status block); make the first call before any stream capture.
  */
 GGEMM_VARK_API int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* c,
                          const float* lhs_scale, const float* rhs_scale,
@@ -97,7 +119,8 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad(const void* lhs, const void* rhs, void* 
  *  m_total       rows allocated in LHS/RHS, or -1 if unknown. When known, group offsets past
  *                m_total are reported (GGEMM_VARK_DEV_BAD_OFFS) and such groups are written
  *                as zeros instead of being read. With m_total == 0, lhs and rhs may be NULL
- *                (every group is empty and C is zeroed).
+ *                (every group is empty and C is zeroed). Unknown (-1): group_offs[G] takes
+ *                m_total's place, as in ggemm_vark_fp8_wgrad, and no load reaches past it.
  *  scale_stride  0: lhs_scale/rhs_scale are single values (the reference's tensorwise scales,
  *                bench.py:266-267); 1: they are arrays of G per-group values.
  *  path          GGEMM_VARK_PATH_* selector.
@@ -122,6 +145,23 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad_ex(const void* lhs, const void* rhs, voi
  */
 GGEMM_VARK_API int ggemm_vark_read_status(void* status, int clear, uint32_t* bits_out);
 
+/*
+ * ggemm_vark_read_status_stream - read the first `nwords` (1..8) words of a status block in
+ * the order of `stream`: the copy is queued behind the stream's earlier work and only that
+ * stream is waited for, so other streams keep running. `clear` then queues, on the same stream,
+ * the zeroing of words 0, 1, 4 and 5. `status` NULL = the current device's library block.
+ */
+GGEMM_VARK_API int ggemm_vark_read_status_stream(void* status, int clear, uint32_t* words_out,
+                                                 int32_t nwords, void* stream);
+
+/*
+ * ggemm_vark_device_bytes - device memory this library has allocated on `device`: 0 until the
+ * first call of an entry point that uses the library's block there, then the 4 KiB status
+ * block. The static array of ggemm_vark_fp8_wgrad_noalloc is not an allocation and is not
+ * counted. Touches no device.
+ */
+GGEMM_VARK_API int ggemm_vark_device_bytes(int32_t device, uint64_t* bytes_out);
+
 /* ggemm_vark_tc_supported - 1 if `path` AUTO would take the tcgen05 path for this layout. */
 GGEMM_VARK_API int ggemm_vark_tc_supported(const void* lhs, const void* rhs, void* c,
                             int32_t OUT_M, int32_t OUT_N,
@@ -141,11 +181,15 @@ GGEMM_VARK_API int ggemm_vark_tc_supported(const void* lhs, const void* rhs, voi
  * GGEMM_VARK_NOALLOC_SCRATCH_BYTES (4 KiB) that every GPU loading this library holds until the
  * process exits. It never calls cudaMalloc or cudaFree.
  *
- *  - Arguments as ggemm_vark_fp8_wgrad_ex; only tensor-core layouts are accepted (16-byte
+ *  - Arguments as ggemm_vark_fp8_wgrad_ex (m_total -1 = unknown: loads stay below
+ *    group_offs[G]); only tensor-core layouts are accepted (16-byte
  *    aligned bases and row pitches, stride_cn == 1, OUT_N a multiple of 8), anything else
  *    returns GGEMM_VARK_ELAYOUT.
- *  - `status`: a caller-owned 16-byte aligned device buffer for the GGEMM_VARK_DEV_* bits, or
- *    NULL to record them in the shared array (cleared at the start of every call, not readable).
+ *  - `status`: a caller-owned 16-byte aligned device buffer of >= 256 bytes for the status
+ *    words, or NULL to record them in the shared array (cleared at the start of every call, not
+ *    readable). Only a caller-owned block lets the caller see a bad group_offs or an expired
+ *    wait; waits are limited to 2 s.
+ *  - lhs and rhs may be NULL when m_total == 0, as for ggemm_vark_fp8_wgrad_ex.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
  *    sets kernel attributes; make that first call before any stream capture.
  *  - All calls on a device share the array and it keeps the last call's contents; calls that
@@ -177,7 +221,8 @@ GGEMM_VARK_API int ggemm_vark_fp8_wgrad_noalloc(const void* lhs, const void* rhs
  *  scales     device fp32 scalars; group_offs device int64 [G + 1]
  * Tensor-core layout rules: 16-byte aligned bases; stride_am, stride_bn, stride_bg and
  * 2 * stride_cm multiples of 16; stride_cn == 1 (GGEMM_VARK_ELAYOUT otherwise). Like the
- * 14-argument wgrad entry point it trusts group_offs to lie inside A and C.
+ * 14-argument wgrad entry point it takes group_offs[G] as the row count of A and C: no load or
+ * store touches a row at or past it, and offsets past it are reported and their expert skipped.
  */
 GGEMM_VARK_API int ggemm_vark_grouped_fp8_fwd(const void* a, const void* b, void* c,
                             const float* a_scale, const float* b_scale,

@@ -116,7 +116,7 @@ def run_gpu(a, b, sa, sb, offs, out=None, status=None, trans_b=True):
 def check(a, b, sa, sb, offs, got, rows=None, trans_b=True):
     ref = vo.grouped_fwd_f32(a, b, sa, sb, offs, rows, trans_b)
     tol = vo.grouped_fwd_tolerance(a, b, sa, sb, offs, ref, rows, trans_b)
-    g = got.float().cpu() if rows is None else got.float().cpu()[rows]
+    g = (got.cpu() if rows is None else got.cpu()[rows]).float()
     err = (g - ref).abs()
     assert bool((err <= tol).all()), f"max excess {float((err - tol).max())}"
     if ref.abs().max() > 0:
@@ -314,8 +314,8 @@ SITES = {  # bench.py:154-181 (M_total = 131072, E = 32)
 @pytest.mark.gpu
 @pytest.mark.parametrize("site", sorted(SITES))
 def test_fwd_full_size_site(site):
-    """Full-size harness site with the reference generator's routing: 8 rows of every expert
-    (first, last and random ones) against the CPU oracle, plus a determinism check."""
+    """Full-size harness site with the reference generator's routing: every row against the CPU
+    oracle's per-element bound (four experts at a time), plus a determinism check."""
     a_dtype, N, K = SITES[site]
     lens = inputs.reference_exponential_lens(32, 131072, seed=42)
     offs = torch.from_numpy(inputs.offsets_from_lens(lens))
@@ -327,13 +327,11 @@ def test_fwd_full_size_site(site):
     out = grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs.cuda())
     torch.cuda.synchronize()
     o = offs.tolist()
-    rng = np.random.default_rng(0)
-    rows = []
-    for e in range(32):
-        if o[e + 1] > o[e]:
-            rows += [o[e], o[e + 1] - 1] + list(rng.integers(o[e], o[e + 1], 6))
-    rows = torch.tensor(sorted(set(rows)))
-    check(a.cpu(), b.cpu(), sa.cpu(), sb.cpu(), offs, out, rows)
+    ac, bc, sac, sbc, oc = a.cpu(), b.cpu(), sa.cpu(), sb.cpu(), out.cpu()
+    for e0 in range(0, 32, 4):
+        rows = torch.arange(o[e0], o[min(32, e0 + 4)])
+        if rows.numel():
+            check(ac, bc, sac, sbc, offs, oc, rows)
     again = grouped_gemm_fp8_tensorwise(a, b, sa, sb, offs.cuda())
     torch.cuda.synchronize()
     assert torch.equal(out, again)

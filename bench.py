@@ -690,38 +690,32 @@ def main():
     t_end = time.perf_counter()
     barrier()
     clocks = sampler.window(t_begin, t_end)
-    # Sustained clocks: the same work continued (untimed) for about half a second.
-    t_s0 = time.perf_counter()
-    while time.perf_counter() - t_s0 < 0.5:
-        for _ in range(10):
-            step()
-        torch.cuda.synchronize()
-    clocks_sustained = sampler.window(t_s0 + 0.2, time.perf_counter())
-    sampler.__exit__()
     ms_local = ev0.elapsed_time(ev1) / args.steps
-    ms = max_over_ranks(ms_local)
-    flops_local = p.flops
-    flops_total = flops_local if pg is None else _sum_over_ranks(pg, flops_local, device)
-    value = flops_total / (ms * 1e-3) / 1e12
-    if _lib.read_status(clear=True) != 0:
-        raise SystemExit("device status flags set during the timed region")
     fp8_peak, _hbm, peak_src = measured_peaks()
 
     # ---- the other wgrad workloads, each timed like the headline (outside its timed region) --
     # N = 1: down_wgrad and the skewed-routing stress problem (BASELINE configs 2 and 3). Every
     # N: the GPT-OSS-120B-shaped problem (config 4: G = 128, M_total = 1048576) split into
     # contiguous expert ranges across the ranks (strong scaling; at N = 1 the whole problem).
+    # Each starts after a short idle, like the headline, so that it is not timed in the power
+    # state the previous workload left behind; its own clock window is recorded.
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
     def time_steps(fn, steps):
         for _ in range(3):
             fn()
+        torch.cuda.synchronize()
+        time.sleep(0.5)
         barrier()
-        ev0.record(stream)
+        t0 = time.perf_counter()
+        e0.record(stream)
         for _ in range(steps):
             fn()
-        ev1.record(stream)
+        e1.record(stream)
         torch.cuda.synchronize()
+        t1 = time.perf_counter()
         barrier()
-        return ev0.elapsed_time(ev1) / steps
+        return e0.elapsed_time(e1) / steps, sampler.window(t0, t1)
 
     other = {}
     if args.config == "gate_up" and not args.no_other:
@@ -735,8 +729,13 @@ def main():
             else:
                 q = inputs.make_problem(name, seed=args.seed, device=device)
             qo = torch.empty(q.G, q.OUT_M, q.OUT_N, dtype=torch.bfloat16, device=device)
-            q_ms = time_steps(lambda: variable_k_wgrad(q.lhs, q.rhs, q.lhs_scale, q.rhs_scale,
-                                                       q.group_offs, out=qo), args.steps)
+            # The 120B split's steps are sized so that its timed region lasts about as long as
+            # the headline's at every N (a rank's share is 1/N of the problem): a much longer
+            # region at N = 1 would run into the power cap and flatter the scaling.
+            q_steps = args.steps if name != "shard120b" else max(2, round(args.steps * world / 8))
+            q_ms, q_clocks = time_steps(lambda: variable_k_wgrad(q.lhs, q.rhs, q.lhs_scale,
+                                                                 q.rhs_scale, q.group_offs,
+                                                                 out=qo), q_steps)
             if name == "shard120b":
                 per_ms = _gather_over_ranks(pg, q_ms, device)
                 per_tok = _gather_over_ranks(pg, float(q.lens.sum()), device)
@@ -748,13 +747,13 @@ def main():
                     "per_rank_ms": per_ms, "per_rank_tokens": [int(v) for v in per_tok],
                     "per_rank_tflops": [2.0 * k * q.OUT_M * q.OUT_N / (m * 1e-3) / 1e12
                                         for k, m in zip(per_tok, per_ms)],
-                    "scaling": "strong", "steps": args.steps,
+                    "scaling": "strong", "steps": q_steps, "clocks": q_clocks,
                     "config": {"G": 128, "M_total": 1048576, "OUT_M": q.OUT_M,
                                "OUT_N": q.OUT_N, "split": "contiguous expert ranges"}}
             else:
                 other[f"{name}_wgrad"] = {
                     "value": q.flops / (q_ms * 1e-3) / 1e12, "unit": "TFLOPS",
-                    "ms_per_step": q_ms, "steps": args.steps,
+                    "ms_per_step": q_ms, "steps": args.steps, "clocks": q_clocks,
                     "frac": q.flops / (q_ms * 1e-3) / 1e12 / fp8_peak,
                     "config": {"G": q.G, "M_total": q.M_total, "OUT_M": q.OUT_M,
                                "OUT_N": q.OUT_N}}
@@ -762,6 +761,22 @@ def main():
             torch.cuda.empty_cache()
         if _lib.read_status(clear=True) != 0:
             raise SystemExit("device status flags set in the other workloads")
+
+    # Sustained clocks: the same work continued (untimed) for about half a second.
+    t_s0 = time.perf_counter()
+    while time.perf_counter() - t_s0 < 0.5:
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize()
+    clocks_sustained = sampler.window(t_s0 + 0.2, time.perf_counter())
+    sampler.__exit__()
+    ms = max_over_ranks(ms_local)
+    flops_local = p.flops
+    flops_total = flops_local if pg is None else _sum_over_ranks(pg, flops_local, device)
+    value = flops_total / (ms * 1e-3) / 1e12
+    if _lib.read_status(clear=True) != 0:
+        raise SystemExit("device status flags set during the timed region")
+    fp8_peak, _hbm, peak_src = measured_peaks()
 
     # ---- end-to-end: pinned host inputs -> device -> kernel -> result back to the host ------
     # Through the host-buffer entry point (HostWgrad): per step, the H2D copy of LHS, RHS, scales

@@ -762,14 +762,24 @@ def main():
         if _lib.read_status(clear=True) != 0:
             raise SystemExit("device status flags set in the other workloads")
 
-    # Sustained clocks: the same work continued (untimed) for about half a second.
+    # Sustained clocks: the same work continued (untimed) for about half a second, with its own
+    # events, so that the line also shows the rate once the power cap has settled the clock.
     t_s0 = time.perf_counter()
+    n_sus = 0
+    ev0.record(stream)
     while time.perf_counter() - t_s0 < 0.5:
         for _ in range(10):
             step()
+        n_sus += 10
         torch.cuda.synchronize()
+    ev1.record(stream)
+    torch.cuda.synchronize()
     clocks_sustained = sampler.window(t_s0 + 0.2, time.perf_counter())
     sampler.__exit__()
+    sus_ms = ev0.elapsed_time(ev1) / n_sus
+    sustained = {"value": p.flops / (sus_ms * 1e-3) / 1e12, "unit": "TFLOPS (this rank)",
+                 "ms_per_step": sus_ms, "steps": n_sus, "sm_mhz": clocks_sustained.get("sm_mhz"),
+                 "what": "the same call repeated for 0.5 s after the timed region, untimed"}
     ms = max_over_ranks(ms_local)
     flops_local = p.flops
     flops_total = flops_local if pg is None else _sum_over_ranks(pg, flops_local, device)
@@ -887,6 +897,7 @@ def main():
                        "l2": "inputs (1.13 GB) >> 126 MB L2; no flush"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
             "clocks": clocks, "clocks_sustained_untimed": clocks_sustained,
+            "sustained_untimed": sustained,
             "gpu_launches": args.steps,
             "gpu_launches_e2e": None if e2e is None else e2e["steps"],
             "other_workloads": other,

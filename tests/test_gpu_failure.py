@@ -51,3 +51,27 @@ def test_expired_wait_is_reported_and_context_survives(path):
     ref = vo.wgrad_torch_f32(p.lhs, p.rhs, p.lhs_scale, p.rhs_scale, p.group_offs)
     assert vo.cosine(good.float().cpu(), ref) >= 0.99999
     assert bool((good[1] == 0).all())
+
+
+def test_status_read_in_stream_order_waits_for_its_stream_only():
+    """ggemm_vark_read_status_stream waits for the given stream alone: with another stream busy
+    for about a second it returns at once, and it sees the words of work queued before it on its
+    own stream (a bad offset recorded by a call just before)."""
+    p = inputs.make_problem("tiny", seed=52, lens=[64, 64], OUT_M=256, OUT_N=256)
+    d = p.to("cuda")
+    bad = torch.tensor([0, 64, 40], dtype=torch.int64, device="cuda")
+    status = torch.zeros(64, dtype=torch.int32, device="cuda")
+    out = torch.empty(2, 256, 256, dtype=torch.bfloat16, device="cuda")
+    busy, mine = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(busy):
+        torch.cuda._sleep(2_000_000_000)  # ~1 s of spinning on the other stream
+    with torch.cuda.stream(mine):
+        vark(d.lhs, d.rhs, d.lhs_scale, d.rhs_scale, bad, out=out, status=status)
+        t0 = time.perf_counter()
+        words = _lib.read_status_words(status.data_ptr(), 8, clear=True, stream=mine.cuda_stream)
+        elapsed = time.perf_counter() - t0
+    assert words[_lib.STATUS_WORD_BITS] & _lib.DEV_BAD_OFFS
+    assert elapsed < 0.5, f"the stream-ordered read waited {elapsed:.2f} s"
+    torch.cuda.synchronize()
+    assert int(status[0].item()) == 0  # cleared in the same stream order

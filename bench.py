@@ -719,7 +719,22 @@ def main():
 
     other = {}
     if args.config == "gate_up" and not args.no_other:
-        from ggemm_asm_b200 import inputs
+        from ggemm_asm_b200 import inputs, launch_raw
+
+        # The reference-facing 14-argument entry point on the same problem: no M_total, so its
+        # loads are bounded by group_offs[G] on the device.
+        def drop_in():
+            launch_raw(p.lhs.data_ptr(), p.rhs.data_ptr(), out.data_ptr(),
+                       p.lhs_scale.data_ptr(), p.rhs_scale.data_ptr(), p.group_offs.data_ptr(),
+                       p.G, p.OUT_M, p.OUT_N, p.lhs.stride(0), p.rhs.stride(0), out.stride(0),
+                       out.stride(1), out.stride(2), stream.cuda_stream)
+
+        d_ms, d_clocks = time_steps(drop_in, args.steps)
+        other["gate_up_wgrad_14arg"] = {
+            "value": _sum_over_ranks(pg, p.flops, device) / (max_over_ranks(d_ms) * 1e-3) / 1e12
+            if pg is not None else p.flops / (d_ms * 1e-3) / 1e12,
+            "unit": "TFLOPS", "ms_per_step": d_ms, "steps": args.steps, "clocks": d_clocks,
+            "api": "ggemm_vark_fp8_wgrad (the 14-argument drop-in, M_total not given)"}
 
         names = (["down", "skew"] if world == 1 else []) + ["shard120b"]
         for name in names:

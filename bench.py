@@ -262,11 +262,11 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    from ggemm_asm_b200 import inputs
-
     torch.set_num_threads(os.cpu_count() or 1)
-    name = workload_name(args.config)
-    p = inputs.make_problem(name, seed=args.seed, device="cpu")
+    # The problem the repo arm's rank 0 runs for this config (routing, shape, --groups/--tokens),
+    # generated on the host: ref_exp keeps the reference's exponential routing, shard120b is the
+    # whole 120B-shaped problem.
+    p, _ = build_problem(args, 0, 1, "cpu")
     for _ in range(args.warmup):
         cpu_sample_step(p)
     flops, t = 0.0, 0.0
@@ -282,7 +282,7 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{name}_wgrad", "G": p.G, "M_total": p.M_total,
+            "config": {"workload": f"{args.config}_wgrad", "G": p.G, "M_total": p.M_total,
                        "OUT_M": p.OUT_M, "OUT_N": p.OUT_N},
             "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": cores, "kind": "port",
                              "sample": sample},

@@ -223,8 +223,8 @@ int run(const void* lhs, const void* rhs, void* c, const float* ls, const float*
   CUtensorMap map_rhs, map_lhs, map_c;  // the single-CTA kernel's maps
   if (pair) {
     // The pair kernel loads a group's ragged last K step as one 32-token chunk, and the B of
-    // its last row tile (LHS) and transposed last column tile (RHS) through narrow boxes when
-    // their B halves fit in 32 or 64 bytes.
+    // its last row tile (LHS) and last column tile (RHS) through narrow boxes when their B
+    // halves fit in 32 or 64 bytes.
     if (!vark::encode_pair_maps(&pm, lhs, rhs, c, G, OUT_M, OUT_N, slm, srm, scg, scm,
                                 token_dim))
       return GGEMM_VARK_ELAYOUT;

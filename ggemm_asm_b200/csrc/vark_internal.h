@@ -105,8 +105,8 @@ size_t tc2_smem_bytes();
 // map_lhs32 / map_rhs32: the same operands with 32-token boxes (a group's ragged last K step).
 // map_lhs_n / map_lhs32_n and map_rhs_n / map_rhs32_n: boxes {w, PAIR_TOKENS} and {w, 32} with
 // the w-byte swizzle, w = p.bw_lhs / p.bw_rhs (32 or 64; any valid map when 0). An item whose
-// B half (MMA N / 2) fits in w bytes loads B through them: the last row tile (B = LHS) and the
-// transposed last column tile (B = RHS).
+// B half (MMA N / 2) fits in w bytes loads B through them: the last row tile (B = LHS, C columns
+// on the TMEM lanes) and the last column tile (B = RHS, C rows on the lanes).
 // Narrow width for a last tile of MMA N = n: 32 or 64 bytes when N / 2 fits, else 0.
 inline int32_t pair_narrow_width(int32_t n) { return n <= 64 ? 32 : (n <= 128 ? 64 : 0); }
 struct PairMaps {

@@ -4,22 +4,26 @@
 // Computes, for every group g, C[g] = sL*sR * LHS[off_g:off_{g+1}]^T . RHS[off_g:off_{g+1}]
 // (ggemm-asm README.md:5,45-48; bench.py:182-193 "dW = lhs^T @ rhs" per expert).
 //
-// Tile and operands. One work item is (group g, 256 columns of C, up to 256 rows of C) and is
-// computed by a cluster of two CTAs with tcgen05.mma.cta_group::2 (M=256, N<=256, K=32):
-//   * MMA-M runs along OUT_N (C columns): operand A = RHS (e5m2). CTA r of the pair holds C
-//     columns [n0 + 128r, n0 + 128r + 128) and its TMEM accumulates those 128 columns (one per
-//     TMEM lane).
-//   * MMA-N runs along OUT_M (C rows): operand B = LHS (e4m3). The N rows of the item are split
-//     N/2 per CTA; the MMA reads both halves across the pair. N is 256 except for the last row
-//     tile, where it is the remaining rows rounded up to 32 (64 for OUT_M = 2880 = 11x256 + 64),
-//     so ragged OUT_M costs no tensor work. Along OUT_N the waste is at most one 128-column half
-//     (2.2% at 5760 = 45 x 128).
-// The last column tile is different when OUT_N is not a multiple of 256 (5760 = 22.5 x 256,
-// 2880 = 11.25 x 256): most of its 256 MMA-M rows would be padding. Those items are computed
-// transposed: MMA-M = 256 runs along OUT_M (A = LHS e4m3, 128 C rows per CTA, one per TMEM lane)
-// and MMA-N along the remaining columns rounded up to 32 (B = RHS e5m2, half per CTA), with a
-// non-transposed epilogue. Same item count and order; the padding shrinks from 256 - E columns
-// per row tile to at most 31 (and the rows of the last row tile, as for any 256-row M tile).
+// Tile and operands. One work item is (group g, up to 256 rows of C, up to 256 columns of C) and
+// is computed by a cluster of two CTAs with tcgen05.mma.cta_group::2 (M=256, N<=256, K=32), in
+// one of two orientations:
+//   * C rows on TMEM lanes, for every item of a full 256-row tile. MMA-M runs along OUT_M:
+//     operand A = LHS (e4m3), CTA r of the pair holds C rows [m0 + 128r, m0 + 128r + 128), one
+//     per TMEM lane. MMA-N runs along OUT_N: operand B = RHS (e5m2), N/2 columns per CTA, the
+//     MMA reading both halves across the pair. N is 256 except in the last column tile, where it
+//     is the remaining columns rounded up to 32 (128 at OUT_N = 5760 = 22 x 256 + 128, 64 at
+//     2880). An epilogue lane holds 32 consecutive columns of one C row: one 64-byte row of the
+//     stored box.
+//   * C columns on TMEM lanes, for the last row tile when OUT_M is not a multiple of 256 (64 rows
+//     at 2880 = 11 x 256 + 64), where most of a 256-row MMA-M would be padding. MMA-M runs along
+//     OUT_N (A = RHS, 128 C columns per CTA) and MMA-N along the tile's rows rounded up to 32
+//     (B = LHS, half per CTA), so ragged OUT_M costs no tensor work. An epilogue lane holds 32
+//     rows of one C column, so the epilogue transposes through shared memory (lane pairs exchange
+//     values so that each lane writes 4-byte words).
+// Either orientation moves the same bytes (2 x 128 x TK per CTA and TK tokens for 128 x 256 x TK
+// MACs); the first takes the cheaper epilogue. Measured against C columns on the lanes for every
+// item (one process, 9 interleaved rounds, bit-identical outputs): gate_up +1.4%, down +1.1%,
+// skewed routing +1.3%, the reference's exponential routing +2.4%.
 // Both operands stay in their token-major layout, which for the MMA is MN-major: a TMA box of
 // 128 contiguous features x TK tokens lands with the 128-byte swizzle of the canonical MN-major
 // layout. Per CTA and TK tokens that is 2 x 128 x TK bytes for 128 x 256 x TK MACs. Boxes that
@@ -28,14 +32,14 @@
 //
 // Warp roles (64 + 32 x EPI_WARPS threads per CTA, one CTA per SM, 74 pairs on 148 SMs,
 // persistent over a static round-robin schedule of work items by cluster):
-//   warp 0      TMA producer (both CTAs): ring of ST stages {RHS 128 x TK, LHS 128 x TK},
+//   warp 0      TMA producer (both CTAs): ring of ST stages {A 128 x TK, B N/2 x TK},
 //               completion counted on the pair leader's full barrier
 //   warp 1      TMEM owner (both CTAs, cta_group::2 allocation of all 512 columns = two
 //               128-lane x 256-column fp32 accumulators); in the leader also the MMA issuer
-//   warps 2..   epilogue (both CTAs): tcgen05.ld 32 TMEM columns (= 32 C rows of this lane's C
-//               column) -> * (sL*sR) -> bf16 (RNE) -> transposed into a 64B-swizzled 32x32 smem
-//               box (lane pairs exchange values so each lane writes 4-byte words) -> TMA store;
-//               warp w owns TMEM lanes 32*(w%4)..+31 = 32 C columns of this CTA's half
+//   warps 2..   epilogue (both CTAs): tcgen05.ld 32 TMEM columns -> * (sL*sR) -> bf16 (RNE)
+//               -> a 64B-swizzled 32x32 smem box -> TMA store; warp w owns TMEM lanes
+//               32*(w%4)..+31 = 32 C rows (or, C columns on the lanes, 32 C columns) of this
+//               CTA's half
 // The leader's commits arrive on both CTAs' barriers (tcgen05.commit multicast); the epilogue
 // warps of both CTAs release an accumulator on the leader's barrier.
 //
@@ -92,8 +96,8 @@ constexpr int ST = PAIR_STAGES;
 constexpr uint32_t BOX_BYTES = 128 * TK;                 // one operand box per CTA
 constexpr int SPB = TK / 32;                             // K steps (MMAs) per full stage
 constexpr uint32_t TAIL_BYTES = 128 * 32;                // one operand's 32-token tail chunk
-// Narrow B: the last row tile (B = LHS) or the transposed last column tile (B = RHS) whose
-// B half (MMA N / 2) fits in 32 or 64 bytes loads B in boxes that wide, with the matching
+// Narrow B: an item whose B half (MMA N / 2) fits in 32 or 64 bytes - the last column tile
+// (B = RHS) or the last row tile (B = LHS) - loads B in boxes that wide, with the matching
 // swizzle, instead of 128 wide: the 128-wide boxes were mostly past the operand's edge (zero
 // fill) yet took the same TMA time per K step. B's token rows are then bw bytes apart.
 constexpr uint32_t ACC_COLS = 256;                       // TMEM columns per accumulator
@@ -107,9 +111,9 @@ static_assert(PAIR_HALF == 128 && ITEM_ROWS == 256, "pair tile is 256 x 256");
 static_assert(TK % 32 == 0 && TK >= 64 && TK <= 256, "token block: a multiple of the MMA K (32), TMA box rows <= 256");
 
 // Shared-memory map (offsets from a 1024-byte aligned base; identical in both CTAs).
-constexpr uint32_t OFF_RHS = 0;                          // operand A stages
-constexpr uint32_t OFF_LHS = OFF_RHS + ST * BOX_BYTES;   // operand B stages
-constexpr uint32_t OFF_EPI = OFF_LHS + ST * BOX_BYTES;
+constexpr uint32_t OFF_A = 0;                            // operand A stages
+constexpr uint32_t OFF_B = OFF_A + ST * BOX_BYTES;       // operand B stages
+constexpr uint32_t OFF_EPI = OFF_B + ST * BOX_BYTES;
 constexpr uint32_t OFF_TAIL = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;  // 2 x {A, B} tails
 constexpr uint32_t OFF_BARS = OFF_TAIL + 2 * 2 * TAIL_BYTES;
 constexpr uint32_t NUM_BARS = 2 * ST + 2 + 2 + 1 + 1 + 2 + 2;
@@ -119,10 +123,11 @@ constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;
 static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 static_assert(OFF_EPI % 1024 == 0 && OFF_TAIL % 1024 == 0, "alignment");
 
-// Instruction descriptors without N: the item's N is or-ed in at run time.
-constexpr uint32_t IDESC_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
-                                             /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
-constexpr uint32_t IDESC_EDGE_NO_N = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
+// Instruction descriptors without N (or-ed in per item): C rows on the TMEM lanes (A = LHS) and
+// C columns on the lanes (A = RHS).
+constexpr uint32_t IDESC_ROWS_NO_N = idesc_f8f6f4(/*A=LHS e4m3*/ 0, /*B=RHS e5m2*/ 1,
+                                                  /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
+constexpr uint32_t IDESC_COLS_NO_N = idesc_f8f6f4(/*A=RHS e5m2*/ 1, /*B=LHS e4m3*/ 0,
                                                   /*A MN-major*/ 1, /*B MN-major*/ 1, 256, 0);
 
 struct Ctl {
@@ -166,11 +171,11 @@ __device__ __forceinline__ bool warp_wait(const Ctl& ctl, uint32_t bar, uint32_t
 struct Item {
   int g, r;        // group, and the item's index within it
   int m0, n0;      // first C row and first C column of the pair tile (set by place_item)
-  int nrows;       // MMA N: C rows of the item, a multiple of 32 (<= 256)
+  int nrows;       // C rows of the item rounded up to 32 (<= 256): MMA N with C columns on lanes
   int tokens;      // K_g (0 for empty or invalid groups)
   int64_t end;     // off_{g+1}
-  bool edge;       // last, partial column tile: computed transposed (see the file comment)
-  int ecols;       // edge item's MMA N: its C columns rounded up to 32
+  bool rows_lanes; // C rows on the TMEM lanes (every full row tile; see the file comment)
+  int ecols;       // C columns of the item rounded up to 32 (<= 256): MMA N with C rows on lanes
   uint32_t bw;     // B bytes per token row in shared memory: 128, or 64 / 32 (narrow maps)
 };
 
@@ -215,10 +220,10 @@ __device__ __forceinline__ Item place_item(const TcParams& p, Item t) {
   t.m0 = (t.r % p.row_tiles) * ITEM_ROWS;
   t.n0 = (t.r / p.row_tiles) * ITEM_COLS;
   t.nrows = min(ITEM_ROWS, (p.OUT_M - t.m0 + 31) & ~31);
-  t.edge = t.n0 + ITEM_COLS > p.OUT_N;
-  t.ecols = (p.OUT_N - t.n0 + 31) & ~31;
-  const int b_half = (t.edge ? t.ecols : t.nrows) >> 1;
-  const int nw = t.edge ? p.bw_rhs : p.bw_lhs;
+  t.rows_lanes = t.m0 + ITEM_ROWS <= p.OUT_M;
+  t.ecols = min(ITEM_COLS, (p.OUT_N - t.n0 + 31) & ~31);
+  const int b_half = (t.rows_lanes ? t.ecols : t.nrows) >> 1;
+  const int nw = t.rows_lanes ? p.bw_rhs : p.bw_lhs;
   t.bw = (nw > 0 && b_half <= nw) ? static_cast<uint32_t>(nw) : 128u;
   return t;
 }
@@ -350,12 +355,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int nkb = (steps + SPB - 1) / SPB;         // main-ring blocks
       // First token of the group as a TMA row coordinate (token_limit <= INT32_MAX).
       const int32_t lo = static_cast<int32_t>(t.end - t.tokens);
-      // A: this CTA's 128 C columns (RHS); B: this CTA's half of the item's rows (LHS). Edge
-      // items swap them: A = 128 C rows (LHS), B = half of the edge columns (RHS). Every N/2 is
-      // a multiple of 16, so the TMA x coordinates stay 16-byte aligned.
+      // C rows on the lanes: A = this CTA's 128 C rows (LHS), B = this CTA's half of the item's
+      // columns (RHS). C columns on the lanes: A = 128 C columns (RHS), B = half of the rows
+      // (LHS). Every N/2 is a multiple of 16, so the TMA x coordinates stay 16-byte aligned.
       const int32_t r = static_cast<int32_t>(rank);
-      const int32_t xa = t.edge ? t.m0 + PAIR_HALF * r : t.n0 + PAIR_HALF * r;
-      const int32_t xb = t.edge ? t.n0 + (t.ecols >> 1) * r : t.m0 + (t.nrows >> 1) * r;
+      const int32_t xa = t.rows_lanes ? t.m0 + PAIR_HALF * r : t.n0 + PAIR_HALF * r;
+      const int32_t xb = t.rows_lanes ? t.n0 + (t.ecols >> 1) * r : t.m0 + (t.nrows >> 1) * r;
       if (ragged != 0) {
         // The tail: one 32-token chunk from the group's last whole step on, into a tail buffer
         // (two, used in turn), loaded first so that its zeroing is long done when the MMA warp
@@ -378,12 +383,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const uint32_t tail_b = t.bw * 32u;
         if (lane == 0) {
           mbar_arrive_expect_tx(bar_zfill, TAIL_BYTES + tail_b);
-          tma_load_2d_hint(ta, t.edge ? &map_lhs32 : &map_rhs32, bar_zfill, xa, y, policy);
+          tma_load_2d_hint(ta, t.rows_lanes ? &map_lhs32 : &map_rhs32, bar_zfill, xa, y, policy);
           tma_load_2d_hint(ta + TAIL_BYTES,
-                           t.edge ? (nb ? &map_rhs32_n : &map_rhs32)
+                           t.rows_lanes ? (nb ? &map_rhs32_n : &map_rhs32)
                                   : (nb ? &map_lhs32_n : &map_lhs32),
                            bar_zfill, xb, y, policy);
-          note_rows(t.edge, static_cast<int64_t>(y) + 32, static_cast<int64_t>(y) + 32);
+          note_rows(t.rows_lanes, static_cast<int64_t>(y) + 32, static_cast<int64_t>(y) + 32);
         }
         ztail = static_cast<int>(tb);
         const uint32_t keep = static_cast<uint32_t>(back ? 32 - ragged : ragged);
@@ -392,10 +397,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         zb0 = back ? 0u : keep * t.bw;
         zb1 = back ? keep * t.bw : tail_b;
       }
-      const CUtensorMap* const map_a = t.edge ? &map_lhs : &map_rhs;
+      const CUtensorMap* const map_a = t.rows_lanes ? &map_lhs : &map_rhs;
       const bool nb = t.bw != 128u;
       const CUtensorMap* const map_b =
-          t.edge ? (nb ? &map_rhs_n : &map_rhs) : (nb ? &map_lhs_n : &map_lhs);
+          t.rows_lanes ? (nb ? &map_rhs_n : &map_rhs) : (nb ? &map_lhs_n : &map_lhs);
       const uint32_t stage_bytes = BOX_BYTES + t.bw * TK;
       for (int kb = 0; kb < nkb; ++kb) {
         // Neither wait depends on the pending tail: the MMA warp takes it after the item's
@@ -413,9 +418,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           int32_t y = lo + TK * kb;
           if (bounded && static_cast<int64_t>(y) + TK > lim) y += 32 * (steps - SPB * kb) - TK;
           mbar_arrive_expect_tx_cluster(fb, stage_bytes);
-          tma_load_2d_pair(base + OFF_RHS + stage * BOX_BYTES, map_a, fb, xa, y, policy);
-          tma_load_2d_pair(base + OFF_LHS + stage * BOX_BYTES, map_b, fb, xb, y, policy);
-          note_rows(t.edge, static_cast<int64_t>(y) + TK, static_cast<int64_t>(y) + TK);
+          tma_load_2d_pair(base + OFF_A + stage * BOX_BYTES, map_a, fb, xa, y, policy);
+          tma_load_2d_pair(base + OFF_B + stage * BOX_BYTES, map_b, fb, xb, y, policy);
+          note_rows(t.rows_lanes, static_cast<int64_t>(y) + TK, static_cast<int64_t>(y) + TK);
         }
         __syncwarp();
         withhold = false;
@@ -477,8 +482,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!warp_wait(ctl, bar_tempty + 8 * acc, acc_phase ^ 1u, 0x200u | acc)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
-        const uint32_t idesc = t.edge ? IDESC_EDGE_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
-                                      : IDESC_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
+        const uint32_t idesc =
+            t.rows_lanes ? IDESC_ROWS_NO_N | (static_cast<uint32_t>(t.ecols >> 3) << 17)
+                         : IDESC_COLS_NO_N | (static_cast<uint32_t>(t.nrows >> 3) << 17);
         // Descriptors without their start address, built once per item. A: 32 token rows of 128
         // bytes per K step. B: 32 token rows of bw bytes with the bw-byte swizzle, 8-row K groups
         // 8 * bw bytes apart. A K step adds its byte offset / 16 to the address field (the
@@ -494,8 +500,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after_sync();
-          const uint32_t a_stage = base + OFF_RHS + stage * BOX_BYTES;
-          const uint32_t b_stage = base + OFF_LHS + stage * BOX_BYTES;
+          const uint32_t a_stage = base + OFF_A + stage * BOX_BYTES;
+          const uint32_t b_stage = base + OFF_B + stage * BOX_BYTES;
           if (lane == 0) {
             const int ks_n = kb < nkb - 1 ? SPB : steps - SPB * (nkb - 1);
             const uint64_t a0 = a_fixed | (a_stage >> 4);
@@ -577,13 +583,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     for (int item = cluster; item < num_items; item += nclusters) {
       const Item t = place_item(p, nxt);
       if (item + nclusters < num_items) nxt = decode_item(p, lim, item + nclusters, reporter);
-      // This warp's 32 TMEM lanes are 32 C columns starting at xcol (normal items) or 32 C rows
-      // starting at row0 (edge items); TMEM column chunk c is 32 C rows (normal) or 32 C
-      // columns (edge) of those.
+      // This warp's 32 TMEM lanes are 32 C rows starting at row0 (C rows on the lanes) or 32 C
+      // columns starting at xcol; TMEM column chunk c is 32 C columns or 32 C rows of those.
       const int xcol = t.n0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;
       const int row0 = t.m0 + PAIR_HALF * static_cast<int>(rank) + quarter * 32;
-      const bool live = t.edge ? row0 < p.OUT_M : xcol < p.OUT_N;
-      const int span = t.edge ? min(t.ecols, p.OUT_N - t.n0) : min(t.nrows, p.OUT_M - t.m0);
+      const bool live = t.rows_lanes ? row0 < p.OUT_M : xcol < p.OUT_N;
+      const int span = t.rows_lanes ? min(t.ecols, p.OUT_N - t.n0) : min(t.nrows, p.OUT_M - t.m0);
       const int nchunks = (span + 31) / 32;
       if (t.tokens == 0) {
         if (live) {
@@ -598,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             for (int c = half; c < nchunks; c += EPI_SPLIT) {
-              if (t.edge)
+              if (t.rows_lanes)
                 tma_store_3d(&map_c, buf, t.n0 + c * EPI_COLS, row0, t.g);
               else
                 tma_store_3d(&map_c, buf, xcol, t.m0 + c * EPI_ROWS, t.g);
@@ -624,9 +629,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const uint32_t odd = static_cast<uint32_t>(lane) & 1u;
         auto emit = [&](uint32_t (&r)[32], int c) {
           const uint32_t buf = next_buf();
-          if (t.edge) {
-            // Edge item: this lane holds 32 consecutive C columns of C row row0 + lane: one
-            // 64-byte row of the box, four 16-byte pieces at the 64-byte swizzle's positions.
+          if (t.rows_lanes) {
+            // C rows on the lanes: this lane holds 32 consecutive C columns of C row row0 + lane:
+            // one 64-byte row of the box, four 16-byte pieces at the 64-byte swizzle's positions.
             const uint32_t row = static_cast<uint32_t>(lane);
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {

@@ -620,9 +620,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after_sync();
       if (live) {
         const uint32_t t_acc = tmem_base + lane_field + acc * ACC_COLS;
-        // This lane holds C column xcol + lane for the 32 C rows of TMEM columns [32c, 32c+32).
         // The 32x32 box is stored row-major (64-byte rows) with the 64-byte swizzle the C tensor
-        // map expects (16-byte chunk ^= (row >> 1) & 3). Lanes 2i and 2i+1 (columns 2i, 2i+1)
+        // map expects (16-byte chunk ^= (row >> 1) & 3). With C columns on the lanes, this lane
+        // holds C column xcol + lane for the 32 C rows of TMEM columns [32c, 32c+32); lanes 2i
+        // and 2i+1 (columns 2i, 2i+1)
         // swap one value per row pair so that each writes a 4-byte word of one row: the even
         // lane row j, the odd lane row j+1 - 32 lanes cover two 64-byte rows, no bank conflict.
         const uint32_t pr = static_cast<uint32_t>(lane) >> 1;  // column pair index i

@@ -17,15 +17,14 @@
 //  - A CTA reduces the amax of its slice of unit u, publishes it (one atomicMax on the unit's
 //    word, then an arrival count), waits until every CTA has published, and quantises the same
 //    slice. All CTAs hold equal shares of a unit, so the wait is short.
-//  - The second read of a row mostly comes from L2: the distance between the two reads is about
-//    one unit (up to ~47 MB at 4096 x 5760 bf16) and B200's L2 is 126 MB. Measured DRAM reads:
-//    exactly the input size when a unit's quantise pass directly follows its amax pass, 1.23x
-//    the input with the interleaved order below (which keeps HBM reading while stores drain).
-//  - Contiguous rows (the usual layout): one producer warp streams the CTA's slices through a
-//    ring of shared-memory chunks with 1-D bulk copies (cp.async.bulk), running ahead across the
-//    amax/quantise boundary; the 16 consumer warps release chunks through mbarriers and meet at
-//    a CTA barrier only a few times per unit. Other layouts (padded rows, unaligned bases,
-//    F % 8 != 0) take a register-load kernel with the same schedule and results.
+//  - The second read of a row mostly comes from L2: at most about two units (up to ~94 MB at
+//    4096 x 5760 bf16) lie between the two reads, and B200's L2 is 126 MB.
+//  - Contiguous rows (the usual layout): the consumer warps work in two roles at once, 4 warps
+//    reducing the amax of unit u from one ring of shared-memory chunks while 12 warps quantise
+//    unit u-1 from a second ring; a producer warp per ring streams the CTA's slices into it with
+//    1-D bulk copies (cp.async.bulk), and chunks are released through mbarriers. Other layouts
+//    (padded rows, unaligned bases, F % 8 != 0) take a register-load kernel with the one-role
+//    schedule and the same results.
 //  - The quotient x / s is exact without a division per element (Markstein's correction below).
 //  - Every wait is bounded (globaltimer): on expiry the CTA records GGEMM_VARK_DEV_TIMEOUT, raises
 //    an abort word in the workspace that the other CTAs' waits watch, and returns.
@@ -44,39 +43,41 @@ constexpr int kThreads = 512;  // threads doing the arithmetic (register-load ke
 constexpr int kUnroll = 4;
 constexpr int kWarps = kThreads / 32;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
-// Bulk-copy kernel: kQtThreads consumer threads plus one producer warp, and a ring of QT_STAGES
-// chunks of at most QT_CHUNK bytes, one CTA per SM. 64 KB x 3 measured fastest at the gate_up
-// shapes: against 32 KB x 3 with two CTAs per SM it takes 11% less time on x [131072, 2880], 13%
-// less on dy [131072, 5760] and 8% less on dy under skewed routing (half as many CTAs meet in
-// each unit's grid-wide wait, and fewer hand-offs per byte); 48 KB x 4, 56 or 72 KB x 3 and
-// 1024 consumer threads were slower, and 96 KB x 2 was faster on x alone but 9% slower on dy.
-#ifndef VARK_QT_CONSUMERS
-#define VARK_QT_CONSUMERS 512
-#endif
-constexpr int kQtThreads = VARK_QT_CONSUMERS;  // consumer threads of the bulk-copy kernel
+// Bulk-copy kernel (contiguous rows), one CTA per SM: 16 consumer warps in two roles plus one
+// producer warp per role. WS_AMAX_WARPS warps reduce the amax of unit s from the "amax ring"
+// (WS_A_STAGES chunks of up to WS_A_CAP bytes: the first, DRAM read of every chunk) while the
+// other warps quantise unit s-1 from the "quantise ring" (WS_Q_STAGES chunks of up to WS_Q_CAP
+// bytes: the re-read, mostly from L2). Shapes measured in one process at the gate_up shapes
+// (x [131072, 2880], dy [131072, 5760], and dy under skewed routing; ms; bit-identical output):
+//   all 16 warps on each chunk in turn, one ring of 64 KB x 3 (96 KB x 2 for x)
+//                                                            0.291 / 0.501 / 0.613
+//   4 amax warps, amax ring 40 KB x 2, quantise ring 64 KB x 2 (kept)   0.226 / 0.446 / 0.567
+//   4 amax warps, 48 KB x 2 each                                        0.231 / 0.487 / 0.577
+//   4 amax warps, 32 KB x 2 and 64 KB x 2                               0.242 / 0.443 / 0.573
+//   3 amax warps, 40 KB x 2 and 56 KB x 2                               0.233 / 0.455 / 0.578
+//   2 amax warps, 48 KB x 2 each                                        0.248 / 0.460 / 0.581
+//   quantise chunks of 24 or 32 KB (amax 48 KB x 3 or 32 KB x 4)       0.244-0.291 / 0.56-0.63
+// With one set of warps on every chunk, the amax reads (DRAM latency, little arithmetic) and
+// the quantisation (L2 reads, most of the arithmetic) took turns on the SM instead of
+// overlapping; the quantise ring wants the larger chunks.
+constexpr int kQtThreads = 512;                   // consumer threads (both roles)
 constexpr int kQtWarps = kQtThreads / 32;
-static_assert(kQtThreads % 32 == 0 && kQtThreads + 32 <= 1024, "bulk-copy kernel block size");
-constexpr int kTmaThreads = kQtThreads + 32;
-#ifndef VARK_QT_CHUNK
-#define VARK_QT_CHUNK 65536
-#endif
-#ifndef VARK_QT_STAGES
-#define VARK_QT_STAGES 3
-#endif
-constexpr uint32_t QT_CHUNK = VARK_QT_CHUNK;
-static_assert(QT_CHUNK % 16 == 0, "chunk: whole 16-byte vectors");
-constexpr int QT_STAGES = VARK_QT_STAGES;
-constexpr size_t QT_SMEM = static_cast<size_t>(QT_STAGES) * QT_CHUNK + 2 * QT_STAGES * 8 + 128;
-// The same shared memory as a ring of 2 chunks of up to 1.5 x QT_CHUNK. The host takes it when a
-// CTA's average slice of a unit fits in two such chunks. At the gate_up shapes x (slices of
-// ~159 KB) takes it: 0.299 ms against 0.328 ms with 64 KB x 3, measured in one process; dy
-// (~318 KB), for which 96 KB x 2 measured 0.552 ms against 0.499, keeps 64 KB x 3.
-// The kernel is instantiated per ring (NS stages of ring_cap<NS>() bytes): the stage index and
-// phase of every chunk then come from divisions by a constant.
-constexpr int QT_STAGES_WIDE = 2;
-template <int NS>
-constexpr uint32_t ring_cap() { return static_cast<uint32_t>(QT_STAGES * QT_CHUNK / NS); }
-static_assert(ring_cap<QT_STAGES_WIDE>() % 16 == 0 && QT_STAGES_WIDE <= QT_STAGES, "wide ring");
+constexpr int WS_AMAX_WARPS = 4;
+constexpr int WS_QUANT_WARPS = kQtWarps - WS_AMAX_WARPS;
+constexpr int WS_AMAX_THREADS = 32 * WS_AMAX_WARPS;
+constexpr int WS_QUANT_THREADS = 32 * WS_QUANT_WARPS;
+constexpr int WS_THREADS = kQtThreads + 64;       // + one producer warp per ring
+constexpr int WS_A_STAGES = 2, WS_Q_STAGES = 2;
+constexpr uint32_t WS_A_CAP = 40u * 1024u, WS_Q_CAP = 64u * 1024u;
+// The amax warps take unit s once the quantise warps have finished unit s - WS_LEAD: about two
+// units lie between the two reads of a unit, and every wait points at a lower unit index. A lead
+// of 3 measured dy -2 to -10% (more second reads missing L2), skewed dy +3 to +4%.
+constexpr int WS_LEAD = 2;
+constexpr size_t WS_SMEM = static_cast<size_t>(WS_A_STAGES) * WS_A_CAP +
+                           static_cast<size_t>(WS_Q_STAGES) * WS_Q_CAP +
+                           16 * (WS_A_STAGES + WS_Q_STAGES) + 128;
+static_assert(WS_A_CAP % 16 == 0 && WS_Q_CAP % 16 == 0, "chunks: whole 16-byte vectors");
+static_assert(WS_QUANT_WARPS > 0 && WS_SMEM <= 220 * 1024, "one CTA per SM, both rings");
 
 struct QuantParams {
   const uint8_t* x;          // bf16 rows
@@ -410,28 +411,16 @@ __global__ void __launch_bounds__(kThreads) vark_quant_kernel(const QuantParams 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Bulk-copy kernel (contiguous rows). A CTA works through stages: stage 0 reads its slice of
-// unit 0 (amax); stage s = 1..U interleaves, chunk by chunk (amax reads QT_LEAD chunks ahead),
-// the amax read of its slice of unit s with the quantise read of its slice of unit s-1 (whose scale is known once every CTA has
-// published unit s-1). So HBM serves the first reads of one unit while the fp8 stores of the
-// previous one stream out, and L2 holds about one unit: the quantise reads of unit s-1 (evict
-// first) free the lines the amax reads of unit s fill. (Alternatives measured at 4096 x 5760:
-// all of unit u+1 before unit u's quantise pass thrashed L2; amax then quantise of the same unit
-// kept L2 but left HBM alternating between reading and writing.) One producer warp issues the
-// chunk copies in the same order, QT_STAGES ahead.
+// Bulk-copy kernel (contiguous rows). Every CTA reads its slice of each unit twice: the amax
+// warps reduce the slice of unit s (first read, evict-last so that the lines stay in L2), and
+// once every CTA has published unit s the quantise warps quantise the same slice (second read,
+// evict-first, mostly from L2), while the amax warps already read unit s+1. So HBM serves the
+// first reads of one unit while the second reads and the fp8 stores of the previous one go on.
+// (Alternatives measured at 4096 x 5760: all of unit u+1 before unit u's quantise pass thrashed
+// L2; amax then quantise of the same unit kept L2 but left HBM alternating between reading and
+// writing.) Each role has its own ring and producer warp, which issues its chunk copies in the
+// role's order, a ring ahead.
 // ---------------------------------------------------------------------------------------------
-
-// Order of the chunks within a stage: the amax reads of unit s run QT_LEAD chunks ahead of the
-// quantise reads of unit s-1, so the wait for unit s-1's scale overlaps real work (it costs
-// QT_LEAD chunks per CTA of extra L2 footprint, ~19 MB over 148 CTAs at 64 KB x 2). The quantise
-// pass takes a unit's chunks oldest first; newest first measured 4-11% slower.
-#ifndef VARK_QT_LEAD
-#define VARK_QT_LEAD 2
-#endif
-constexpr int64_t QT_LEAD = VARK_QT_LEAD;
-__device__ __forceinline__ bool amax_next(int64_t ta, int64_t tb, int64_t na, int64_t nb) {
-  return ta < na && (tb == nb || ta < tb + QT_LEAD);
-}
 
 // This CTA's slice of unit w: byte range [b0, b1), whether the unit is valid and non-empty, and
 // its cut into n chunks of cb bytes (the last one shorter). The chunks are as equal as 16-byte
@@ -466,9 +455,10 @@ __device__ __forceinline__ void cut_slice(Slice& sl) {
   sl.n = (len + cb - 1) / cb;  // every chunk non-empty
 }
 
-template <int NS>
+// The slice of unit w cut for a ring of CAP-byte chunks (both roles cover the same bytes).
+template <uint32_t CAP>
 __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
-  Slice sl{0, 0, false, 0, ring_cap<NS>()};
+  Slice sl{0, 0, false, 0, CAP};
   if (w < 0 || w >= p.units) return sl;
   int64_t lo, hi;
   if (!unit_rows(p, w, &lo, &hi) || hi == lo) return sl;
@@ -478,7 +468,7 @@ __device__ __forceinline__ Slice slice_info(const QuantParams& p, int w) {
   sl.b0 = lo * p.stride_x + v0 * 16;
   sl.b1 = lo * p.stride_x + v1 * 16;
   sl.unit_ok = true;
-  cut_slice<ring_cap<NS>()>(sl);
+  cut_slice<CAP>(sl);
   return sl;
 }
 
@@ -491,252 +481,238 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, uint64_t
   return true;
 }
 
-// Barrier 1 joins the kQtThreads consumer threads only (the producer warp never takes part).
-__device__ __forceinline__ bool consumers_sync_or(bool v) {
+// Named barrier over one role's warps (ID 1: amax warps, 2: quantise warps; the producer warps
+// never take part), returning the OR of a flag.
+template <int ID, int N>
+__device__ __forceinline__ bool group_sync_or(bool v) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(kQtThreads)
+      : "r"(static_cast<uint32_t>(v)), "n"(ID), "n"(N)
       : "memory");
   return r != 0;
 }
-
-__device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kQtThreads) : "memory");
+template <int ID, int N>
+__device__ __forceinline__ void group_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(N) : "memory");
 }
 
-// Producer warp, lane 0: issue every chunk in the consumers' order once its stage is free;
-// before returning, let the last copy of every stage land (the CTA's shared memory must outlive
-// it).
-template <int NS>
-struct Producer {
-  const QuantParams& p;
-  uint32_t stage0;
-  uint64_t* full;
-  uint64_t* empty;
-  uint64_t pol_keep, pol_last;
-  int64_t n = 0;  // chunks issued
+// One ring's producer (lane 0 of its warp): every chunk of every unit in order, each into its
+// stage once the role's warps have released it; before returning, let the last copy into every
+// stage land (the CTA's shared memory must outlive it).
+template <uint32_t CAP, int NST>
+__device__ void produce(const QuantParams& p, uint32_t stage0, uint64_t* full, uint64_t* empty,
+                        uint64_t pol, uint32_t where) {
+  int64_t n = 0;
   bool ok = true;
-  __device__ __forceinline__ void issue(const Slice& sl, int64_t t, bool first_read) {
-    if (!ok) return;
-    constexpr int64_t ns = NS;
-    const int k = static_cast<int>(n % ns);
-    if (n >= ns &&
-        !wait_bar(smem_u32(empty + k), static_cast<uint32_t>((n / ns - 1) & 1),
-                  p.timeout_ns)) {
-      report_timeout(p, 0x53000000u);
-      ok = false;
-      return;
-    }
-    const uint32_t bytes = sl.chunk_bytes(t);
-    const uint32_t bar = smem_u32(full + k);
-    mbar_arrive_expect_tx(bar, bytes);
-    bulk_load_1d(stage0 + k * ring_cap<NS>(), p.x + sl.b0 + sl.chunk_offset(t), bytes, bar,
-                 first_read ? pol_keep : pol_last);
-    ++n;
-  }
-  __device__ void run() {
-    Slice a = slice_info<NS>(p, 0);
-    for (int64_t t = 0; t < a.chunks(); ++t) issue(a, t, true);
-    for (int s = 1; s <= p.units && ok; ++s) {
-      const Slice b = slice_info<NS>(p, s - 1);
-      a = slice_info<NS>(p, s);
-      const int64_t na = a.chunks(), nb = b.chunks();
-      for (int64_t ta = 0, tb = 0; ta < na || tb < nb;) {
-        if (amax_next(ta, tb, na, nb))
-          issue(a, ta++, true);
-        else
-          issue(b, tb++, false);
+  for (int s = 0; s < p.units && ok; ++s) {
+    const Slice sl = slice_info<CAP>(p, s);
+    for (int64_t t = 0; t < sl.chunks(); ++t) {
+      const int k = static_cast<int>(n % NST);
+      if (n >= NST &&
+          !wait_bar(smem_u32(empty + k), static_cast<uint32_t>((n / NST - 1) & 1), p.timeout_ns)) {
+        report_timeout(p, where);
+        ok = false;
+        break;
       }
+      const uint32_t bytes = sl.chunk_bytes(t);
+      const uint32_t bar = smem_u32(full + k);
+      mbar_arrive_expect_tx(bar, bytes);
+      bulk_load_1d(stage0 + k * CAP, p.x + sl.b0 + sl.chunk_offset(t), bytes, bar, pol);
+      ++n;
     }
-    constexpr int64_t ns = NS;
-    for (int64_t c = n > ns ? n - ns : 0; c < n; ++c)
-      wait_bar(smem_u32(full + static_cast<int>(c % ns)), static_cast<uint32_t>((c / ns) & 1),
-               p.timeout_ns);
   }
-};
+  for (int64_t c = n > NST ? n - NST : 0; c < n; ++c)
+    wait_bar(smem_u32(full + static_cast<int>(c % NST)), static_cast<uint32_t>((c / NST) & 1),
+             p.timeout_ns);
+}
 
-// Consumer warps (kQtThreads threads): the same chunk order as the producer.
-template <bool E5M2, int NS>
-struct Consumer {
-  const QuantParams& p;
-  uint8_t* stages;
-  uint64_t* full;
-  uint64_t* empty;
-  uint32_t* red;       // kQtWarps words
-  int lane, warp;
-  int64_t j = 0;       // chunks consumed
-  bool fail = false;
-  bool withhold, first_arrival = true;
-  uint32_t m2 = 0;     // running amax (two 16-bit halves) of the current amax slice
-  float scale = 1.0f, recip = 1.0f;
-  bool fast = true;
+// Thread 0 of the amax warps: wait until this CTA's quantise warps have finished unit u.
+__device__ __forceinline__ bool wait_quantised(const QuantParams& p, const volatile int* q_done,
+                                               int u) {
+  if (*q_done >= u) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (*q_done < u) {
+    if (ld_relaxed_u32(p.ws) != 0) return false;  // another CTA gave up
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      report_timeout(p, 0x55000000u | static_cast<uint32_t>(u & 0xffffff));
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
 
-  // Wait for chunk j in its stage (warp-uniform verdict); returns the stage or nullptr.
-  __device__ __forceinline__ const uint4* acquire(int* k_out) {
-    constexpr int64_t ns = NS;
-    const int k = static_cast<int>(j % ns);
-    *k_out = k;
-    if (!__all_sync(0xffffffffu, wait_bar(smem_u32(full + k),
-                                          static_cast<uint32_t>((j / ns) & 1),
-                                          p.timeout_ns)))
-      return nullptr;
-    return reinterpret_cast<const uint4*>(stages + k * ring_cap<NS>());
-  }
-  __device__ __forceinline__ void release(int k) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(empty + k));
-    ++j;
-  }
-  __device__ __forceinline__ void amax_chunk(const Slice& sl, int64_t t) {
-    if (fail) return;
-    int k;
-    const uint4* st = acquire(&k);
-    if (st == nullptr) {
-      fail = true;
-      return;
+// The amax warps (threads [0, WS_AMAX_THREADS)): unit by unit, the amax of this CTA's slice,
+// published by thread 0 (which also records invalid or empty units).
+__device__ void amax_role(const QuantParams& p, const uint8_t* stages, uint64_t* full,
+                          uint64_t* empty, uint32_t* red, const volatile int* q_done) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool withhold = test_withhold(p);
+  bool first_arrival = true, fail = false;
+  int64_t j = 0;  // chunks consumed
+  for (int s = 0; s < p.units; ++s) {
+    const Slice a = slice_info<WS_A_CAP>(p, s);
+    if (!a.unit_ok && blockIdx.x == 0 && tid == 0) {
+      int64_t lo, hi;
+      if (!unit_rows(p, s, &lo, &hi) && p.status != nullptr)
+        atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
+      p.scales[s] = 1.0f;  // invalid or empty unit
     }
-    const uint32_t nv = sl.chunk_bytes(t) / 16;
+    if (s >= WS_LEAD) {
+      bool ok = true;
+      if (tid == 0) ok = wait_quantised(p, q_done, s - WS_LEAD);
+      fail = group_sync_or<1, WS_AMAX_THREADS>(fail || !ok);
+      if (fail) break;
+    }
+    uint32_t m2 = 0;  // two 16-bit maxima of |bf16| bit patterns side by side
+    for (int64_t t = 0; t < a.chunks(); ++t) {
+      const int k = static_cast<int>(j % WS_A_STAGES);
+      if (!__all_sync(0xffffffffu,
+                      wait_bar(smem_u32(full + k), static_cast<uint32_t>((j / WS_A_STAGES) & 1),
+                               p.timeout_ns))) {
+        fail = true;
+        break;
+      }
+      const uint4* st = reinterpret_cast<const uint4*>(stages + k * WS_A_CAP);
+      const uint32_t nv = a.chunk_bytes(t) / 16;
 #pragma unroll 4
-    for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads) {
-      const uint4 x = st[v];
-      m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
-      m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
-      m2 = __vmaxu2(m2, x.z & 0x7fff7fffu);
-      m2 = __vmaxu2(m2, x.w & 0x7fff7fffu);
+      for (uint32_t v = tid; v < nv; v += WS_AMAX_THREADS) {
+        const uint4 x = st[v];
+        m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
+        m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
+        m2 = __vmaxu2(m2, x.z & 0x7fff7fffu);
+        m2 = __vmaxu2(m2, x.w & 0x7fff7fffu);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(empty + k));
+      ++j;
     }
-    release(k);
-  }
-  __device__ __forceinline__ void quant_chunk(const Slice& sl, int64_t t) {
-    if (fail) return;
-    int k;
-    const uint4* st = acquire(&k);
-    if (st == nullptr) {
-      fail = true;
-      return;
+    if (!a.unit_ok) {
+      fail = group_sync_or<1, WS_AMAX_THREADS>(fail);
+      if (fail) break;
+      continue;
     }
-    const uint32_t nv = sl.chunk_bytes(t) / 16;
-    // contiguous rows: element index = byte offset / 2
-    uint2* dst = reinterpret_cast<uint2*>(p.q + (sl.b0 + sl.chunk_offset(t)) / 2);
-    if (fast) {
-#pragma unroll 4
-      for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads)
-        __stcs(dst + v, quant_vec<E5M2, true>(st[v], scale, recip));
-    } else {
-      for (uint32_t v = threadIdx.x; v < nv; v += kQtThreads)
-        __stcs(dst + v, quant_vec<E5M2, false>(st[v], scale, recip));
-    }
-    release(k);
-  }
-  // All consumers: reduce this CTA's amax of unit u and publish it (thread 0). False on failure.
-  __device__ __forceinline__ bool finish_amax(int u) {
     const uint32_t m = __reduce_max_sync(0xffffffffu, max(m2 & 0xffffu, m2 >> 16));
-    m2 = 0;
     if (lane == 0) red[warp] = m;
-    fail = consumers_sync_or(fail);
-    if (fail) return false;
-    uint32_t mm = 0;
-    if (threadIdx.x == 0) {
+    fail = group_sync_or<1, WS_AMAX_THREADS>(fail);
+    if (fail) break;
+    if (tid == 0) {  // the atomics and their fence hold up thread 0 only
+      uint32_t mm = 0;
 #pragma unroll
-      for (int k = 0; k < kQtWarps; ++k) mm = max(mm, red[k]);
-    }
-    consumers_sync();  // red[] may be rewritten after this
-    if (threadIdx.x == 0) {  // the atomics and their fence hold up thread 0 only
-      publish(p, u, mm, withhold && first_arrival);
+      for (int w = 0; w < WS_AMAX_WARPS; ++w) mm = max(mm, red[w]);
+      publish(p, s, mm, withhold && first_arrival);
       first_arrival = false;
     }
-    return true;
+    group_sync<1, WS_AMAX_THREADS>();  // red[] is rewritten for the next unit
   }
-  // All consumers: wait until unit w's amax is complete, then set up its scale.
-  __device__ __forceinline__ bool get_scale(int w) {
-    bool ok = true;
-    if (threadIdx.x == 0) {
-      ok = wait_unit(p, w);
-      if (ok && blockIdx.x == 0)
-        p.scales[w] = unit_scale(ld_relaxed_u32(p.ws + 4 + w), p.fmax);
-    }
-    fail = consumers_sync_or(fail || !ok);
-    if (fail) return false;
-    scale = unit_scale(ld_relaxed_u32(p.ws + 4 + w), p.fmax);
-    recip = __frcp_rn(scale);
-    fast = fast_route_ok(scale);
-    return true;
-  }
-  __device__ __forceinline__ void note_unit(int w, const Slice& sl) {
-    if (sl.unit_ok || blockIdx.x != 0 || threadIdx.x != 0) return;
-    int64_t lo, hi;
-    if (!unit_rows(p, w, &lo, &hi) && p.status != nullptr)
-      atomicOr(p.status, GGEMM_VARK_DEV_BAD_OFFS);
-    p.scales[w] = 1.0f;  // invalid or empty unit
-  }
-  __device__ __forceinline__ void run() {
-    Slice a = slice_info<NS>(p, 0);
-    note_unit(0, a);
-    for (int64_t t = 0; t < a.chunks(); ++t) amax_chunk(a, t);
-    if (a.unit_ok && !finish_amax(0)) return;
-    for (int s = 1; s <= p.units; ++s) {
-      const Slice b = slice_info<NS>(p, s - 1);
-      a = slice_info<NS>(p, s);
-      if (s < p.units) note_unit(s, a);
-      const bool need_scale = b.unit_ok && (b.b1 > b.b0 || blockIdx.x == 0);
-      bool have_scale = false;
-      const int64_t na = a.chunks(), nb = b.chunks();
-      for (int64_t ta = 0, tb = 0; ta < na || tb < nb;) {
-        if (amax_next(ta, tb, na, nb)) {
-          amax_chunk(a, ta++);
-        } else {
-          if (!have_scale) {
-            if (!get_scale(s - 1)) return;
-            have_scale = true;
-          }
-          quant_chunk(b, tb++);
-        }
-      }
-      if (need_scale && !have_scale && !get_scale(s - 1)) return;
-      if (a.unit_ok && !finish_amax(s)) return;
-    }
-    fail = consumers_sync_or(fail);
-  }
-};
+  if (fail && tid == 0) report_timeout(p, 0x52000000u);
+}
 
-template <bool E5M2, int NS>
-// One block per SM (the ring takes ~192 KiB): stating it lets ptxas keep the unrolled consumer
-// loops in registers (without it, it settled at 56 registers and spilled). The loops unrolled by
-// 4, against not unrolled, measured x +1.9 / +2.9%, dy -0.1 / +0.9%, skewed dy +0.9 / +0.6% in two
-// one-process A/B runs with bit-identical output; by 8, dy -7%.
-__global__ void __launch_bounds__(kTmaThreads, 1) vark_quant_tma_kernel(const QuantParams p) {
+// The quantise warps (threads [WS_AMAX_THREADS, kQtThreads)): unit by unit, once every CTA has
+// published the unit's amax, this CTA's slice in fp8; q_done then records the unit.
+template <bool E5M2>
+__device__ void quant_role(const QuantParams& p, const uint8_t* stages, uint64_t* full,
+                           uint64_t* empty, volatile int* q_done) {
+  const int tq = threadIdx.x - WS_AMAX_THREADS, lane = threadIdx.x & 31;
+  bool fail = false;
+  int64_t j = 0;  // chunks consumed
+  for (int s = 0; s < p.units; ++s) {
+    const Slice b = slice_info<WS_Q_CAP>(p, s);
+    float scale = 1.0f, recip = 1.0f;
+    bool fast = true;
+    if (b.unit_ok && (b.chunks() > 0 || blockIdx.x == 0)) {
+      bool ok = true;
+      if (tq == 0) {
+        ok = wait_unit(p, s);
+        if (ok && blockIdx.x == 0) p.scales[s] = unit_scale(ld_relaxed_u32(p.ws + 4 + s), p.fmax);
+      }
+      fail = group_sync_or<2, WS_QUANT_THREADS>(fail || !ok);
+      if (fail) break;
+      scale = unit_scale(ld_relaxed_u32(p.ws + 4 + s), p.fmax);
+      recip = __frcp_rn(scale);
+      fast = fast_route_ok(scale);
+    }
+    for (int64_t t = 0; t < b.chunks(); ++t) {
+      const int k = static_cast<int>(j % WS_Q_STAGES);
+      if (!__all_sync(0xffffffffu,
+                      wait_bar(smem_u32(full + k), static_cast<uint32_t>((j / WS_Q_STAGES) & 1),
+                               p.timeout_ns))) {
+        fail = true;
+        break;
+      }
+      const uint4* st = reinterpret_cast<const uint4*>(stages + k * WS_Q_CAP);
+      const uint32_t nv = b.chunk_bytes(t) / 16;
+      // contiguous rows: element index = byte offset / 2
+      uint2* dst = reinterpret_cast<uint2*>(p.q + (b.b0 + b.chunk_offset(t)) / 2);
+      if (fast) {
+#pragma unroll 4
+        for (uint32_t v = tq; v < nv; v += WS_QUANT_THREADS)
+          __stcs(dst + v, quant_vec<E5M2, true>(st[v], scale, recip));
+      } else {
+        for (uint32_t v = tq; v < nv; v += WS_QUANT_THREADS)
+          __stcs(dst + v, quant_vec<E5M2, false>(st[v], scale, recip));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(empty + k));
+      ++j;
+    }
+    fail = group_sync_or<2, WS_QUANT_THREADS>(fail);
+    if (fail) break;
+    if (tq == 0) *q_done = s;  // every quantise warp is past unit s
+  }
+  if (fail && tq == 0) report_timeout(p, 0x53000000u);
+}
+
+// One CTA per SM (both rings take ~208 KiB): stating it lets ptxas keep the unrolled consumer
+// loops in registers.
+template <bool E5M2>
+__global__ void __launch_bounds__(WS_THREADS, 1) vark_quant_tma_kernel(const QuantParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                              ~static_cast<uintptr_t>(127));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + QT_STAGES * QT_CHUNK);
-  uint64_t* empty = full + QT_STAGES;
-  __shared__ uint32_t red[kQtWarps];
+  uint8_t* stages_a = smem;
+  uint8_t* stages_q = smem + WS_A_STAGES * WS_A_CAP;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(stages_q + WS_Q_STAGES * WS_Q_CAP);
+  uint64_t* empty_a = full_a + WS_A_STAGES;
+  uint64_t* full_q = empty_a + WS_A_STAGES;
+  uint64_t* empty_q = full_q + WS_Q_STAGES;
+  __shared__ uint32_t red[WS_AMAX_WARPS];
+  __shared__ int q_done;  // the last unit this CTA's quantise warps have finished
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
   if (threadIdx.x == 0) {
-    for (int k = 0; k < QT_STAGES; ++k) {
-      mbar_init(smem_u32(full + k), 1);
-      mbar_init(smem_u32(empty + k), kQtWarps);
+    for (int k = 0; k < WS_A_STAGES; ++k) {
+      mbar_init(smem_u32(full_a + k), 1);
+      mbar_init(smem_u32(empty_a + k), WS_AMAX_WARPS);
     }
+    for (int k = 0; k < WS_Q_STAGES; ++k) {
+      mbar_init(smem_u32(full_q + k), 1);
+      mbar_init(smem_u32(empty_q + k), WS_QUANT_WARPS);
+    }
+    q_done = -1;
     fence_mbar_init();
   }
-  __syncthreads();  // the only barrier with the producer warp
+  __syncthreads();  // the only barrier over the whole CTA
   if (warp == kQtWarps) {
-    if (lane == 0) {
-      Producer<NS> pr{p, smem_u32(smem), full, empty, l2_policy_evict_last(),
-                  l2_policy_evict_first()};
-      pr.run();
-    }
+    if (lane == 0)
+      produce<WS_A_CAP, WS_A_STAGES>(p, smem_u32(stages_a), full_a, empty_a,
+                                     l2_policy_evict_last(), 0x54000000u);
     return;
   }
-  Consumer<E5M2, NS> c{p, smem, full, empty, red, lane, warp};
-  c.withhold = test_withhold(p);
-  c.run();
-  if (c.fail && threadIdx.x == 0) report_timeout(p, 0x52000000u);
+  if (warp == kQtWarps + 1) {
+    if (lane == 0)
+      produce<WS_Q_CAP, WS_Q_STAGES>(p, smem_u32(stages_q), full_q, empty_q,
+                                     l2_policy_evict_first(), 0x56000000u);
+    return;
+  }
+  if (warp < WS_AMAX_WARPS)
+    amax_role(p, stages_a, full_a, empty_a, red, &q_done);
+  else
+    quant_role<E5M2>(p, stages_q, full_q, empty_q, &q_done);
 }
 
 }  // namespace
@@ -776,22 +752,10 @@ cudaError_t quant_launch(const uint8_t* x, uint8_t* q, float* scales, const int6
   size_t smem = 0;
   int threads = kThreads;
   if (mode == 2) {
-    // Ring: two wide chunks when a CTA's average slice of a unit fits in them (known row count
-    // only), else the default ring. Either ring takes ~192 KiB of shared memory: one CTA per SM.
-    bool wide = false;
-    if (token_limit != INT64_MAX && p.units > 0) {
-      const double slice = static_cast<double>(token_limit) * static_cast<double>(stride_x_bytes) /
-                           (static_cast<double>(p.units) * sm_count);
-      wide = slice <= 2.0 * ring_cap<QT_STAGES_WIDE>();
-    }
-    if (wide)
-      fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true, QT_STAGES_WIDE>)
-                : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false, QT_STAGES_WIDE>);
-    else
-      fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true, QT_STAGES>)
-                : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false, QT_STAGES>);
-    smem = QT_SMEM;
-    threads = kTmaThreads;
+    fn = e5m2 ? reinterpret_cast<const void*>(&vark_quant_tma_kernel<true>)
+              : reinterpret_cast<const void*>(&vark_quant_tma_kernel<false>);
+    smem = WS_SMEM;
+    threads = WS_THREADS;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
